@@ -1,0 +1,463 @@
+"""Benchmark of the TinyTensor B200 backend.
+
+Headline workload (the one that runs at 1/2/4/8 GPUs): the data-parallel SGD step of
+the 3-layer MLP 1024 -> 4096 (ReLU) -> 4096 (tanh) -> 10 with MSE loss, global batch
+32768 split by rows over the ranks (32768/N each), lr 0.01.  One step = forward +
+symbolic backward (one compiled program) + NCCL sum all-reduce of the weight
+gradients + fused SGD (lr/N).  Total work is fixed as N grows ("strong").
+Synthetic data: X, T ~ N(0,1) seed 4, Xavier-uniform weights seed 4.
+
+At N=1 the line also carries the single-GPU components of the metric (fused
+elementwise GB/s, reductions GB/s, fp32-accurate GEMM TFLOP/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+GLOBAL_BATCH = 32768
+LR = 0.01
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def mlp_flops(rows, with_dx=False):
+    fwd = 2 * rows * (1024 * 4096 + 4096 * 4096 + 4096 * 10)
+    bwd = 2 * fwd if with_dx else 2 * fwd - 2 * rows * 1024 * 4096
+    return fwd + bwd
+
+
+def xavier(rng, fi, fo):
+    lim = np.sqrt(6.0 / (fi + fo))
+    return rng.uniform(-lim, lim, (fi, fo)).astype(np.float32)
+
+
+def mlp_data(seed=4, rows=GLOBAL_BATCH):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, 1024)).astype(np.float32)
+    t = rng.standard_normal((rows, 10)).astype(np.float32)
+    w = [xavier(rng, 1024, 4096), xavier(rng, 4096, 4096), xavier(rng, 4096, 10)]
+    return x, t, w
+
+
+def mlp_graph(tt, rows):
+    g = tt.Graph()
+    X, T = g.input([rows, 1024], name="X"), g.input([rows, 10], name="T")
+    W1, W2, W3 = g.input([1024, 4096], name="W1"), g.input([4096, 4096], name="W2"), g.input([4096, 10], name="W3")
+    h1 = tt.relu(X @ W1)
+    h2 = tt.tanh(h1 @ W2)
+    d = h2 @ W3 - T
+    loss = tt.mean(d * d)
+    return g, (X, T, W1, W2, W3), loss
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait()
+        self.f.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax = float(parts[2])
+                except ValueError:
+                    continue
+                for nm, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# --------------------------------------------------------------------------------------------
+# B200 arm
+# --------------------------------------------------------------------------------------------
+
+def run_b200(args):
+    import torch
+
+    import tinytensor_b200 as tt
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torch.distributed.run")
+    torch.cuda.set_device(local)
+    tt.device_init(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    peaks, peak_src = load_peaks()
+
+    rows = GLOBAL_BATCH // world
+    r0 = rank * rows
+    x, t, w = mlp_data()
+    xs, ts = x[r0:r0 + rows], t[r0:r0 + rows]
+    g, (X, T, W1, W2, W3), loss = mlp_graph(tt, rows)
+    prog = tt.compile_gradients(g, loss, [W1, W2, W3], device=local)
+    stream = tt.Stream()
+    tstream = torch.cuda.ExternalStream(stream.handle)
+    dx, dt = tt.DeviceBuffer.from_numpy(xs), tt.DeviceBuffer.from_numpy(ts)
+    dw = [tt.DeviceBuffer.from_numpy(a) for a in w]
+    # gradients written into one contiguous buffer so a single all-reduce covers them
+    sizes = [a.size for a in w]
+    gbuf = tt.DeviceBuffer([sum(sizes)])
+    offs = np.cumsum([0] + sizes)[:-1]
+    gptr = [gbuf.ptr + int(o) * 4 for o in offs]
+    dloss = tt.DeviceBuffer([])
+    comm = tt.Communicator.from_torch_distributed(local) if world > 1 else None
+    opt = tt.SGD(dw, lr=LR)
+
+    def step():
+        prog.run_device([dx, dt] + dw, [dloss] + gptr, stream)
+        if comm is not None:
+            comm.allreduce_sum(gbuf.ptr, int(sum(sizes)), stream)
+        opt.step(gptr, stream, lr_scale=1.0 / world)
+
+    def barrier():
+        torch.cuda.synchronize()
+        stream.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        tv = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tv, op=dist.ReduceOp.MAX)
+        return float(tv.item())
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    prog.set_profiling(True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = tt.launch_count()
+    barrier()
+    ev0.record(tstream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(tstream)
+    barrier()
+    launches = tt.launch_count() - n0
+    ms = ev0.elapsed_time(ev1) / args.steps
+    clk = clocks.stop()
+    ms = max_over_ranks(ms)
+    prof = prog.profile()
+    prog.set_profiling(False)
+    assert prog.status() == 0
+
+    # end to end through the public API: per step H2D of this rank's (X, T) shard from
+    # pinned host memory, the step, D2H of the loss.
+    px, pt = tt.PinnedBuffer(xs.shape), tt.PinnedBuffer(ts.shape)
+    px.array[...] = xs
+    pt.array[...] = ts
+    hloss = tt.PinnedBuffer([1])
+    from tinytensor_b200 import _lib
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(tstream)
+    for _ in range(args.steps):
+        _lib.check(_lib.lib.tt_memcpy(dx.ptr, px.ptr, dx.nbytes, _lib.H2D, stream.handle))
+        _lib.check(_lib.lib.tt_memcpy(dt.ptr, pt.ptr, dt.nbytes, _lib.H2D, stream.handle))
+        step()
+        _lib.check(_lib.lib.tt_memcpy(hloss.ptr, dloss.ptr, 4, _lib.D2H, stream.handle))
+    e1.record(tstream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    # dominant kernel of the step and its roofline
+    labels = {}
+    for lbl, t_ms in prof:
+        labels.setdefault(lbl, []).append(t_ms)
+    top_lbl, top_ms = max(prof, key=lambda p: p[1])
+    gemm_flops = None
+    if top_lbl.startswith("gemm"):
+        dims = top_lbl.split("[")[1].split()[0].split("x")
+        m, n, k = (int(v) for v in dims)
+        gemm_flops = 2.0 * m * n * k
+    tf32_peak = peaks["bf16_tflops"] / 2.0
+    eff_peak = tf32_peak / 3.0  # 3xTF32: three TF32 products per fp32-accurate product
+    roofline = {
+        "kernel": top_lbl,
+        "bound": "tensor",
+        "achieved": round(gemm_flops / (top_ms * 1e-3) / 1e12, 2) if gemm_flops else None,
+        "peak": round(eff_peak, 1),
+        "unit": "TFLOP/s",
+        "frac": round(gemm_flops / (top_ms * 1e-3) / 1e12 / eff_peak, 4) if gemm_flops else None,
+        "traffic": None,
+        "peak_source": f"{peak_src}: bf16_tflops/2 (TF32) /3 (3xTF32 products), fp32-equivalent",
+        "avg_ms": round(top_ms, 4),
+    }
+    step_flops = mlp_flops(GLOBAL_BATCH)
+    out = {
+        "metric": "MLP DP SGD step/s (1024-4096-4096-10, global batch 32768)",
+        "value": round(1000.0 / ms, 4),
+        "unit": "step/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32 (3xTF32 tensor-core GEMM, fp32 accumulate)",
+        "data": "synthetic: X,T ~ N(0,1) seed 4; Xavier-uniform weights seed 4",
+        "config": {"workload": "mlp_dp_sgd_step", "model": "MLP 1024-4096-4096-10 MSE", "global_batch": GLOBAL_BATCH,
+                   "per_gpu_batch": rows, "lr": LR, "parallelism": f"dp{world}",
+                   "l2": "inputs larger than L2 (activations 512 MiB at N=1, weights 84 MB)",
+                   "tflops_per_step": round(step_flops / 1e12, 4)},
+        "tflops": round(step_flops / (ms * 1e-3) / 1e12, 2),
+        "e2e": {"value": round(1000.0 / e2e_ms, 4), "unit": "step/s",
+                "h2d_bytes_per_step": int(dx.nbytes + dt.nbytes) * world, "d2h_bytes_per_step": 4 * world},
+        "gpu_launches": int(launches),
+        "roofline": roofline,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_components:
+        out["components"] = components(tt, torch, args, peaks, peak_src)
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        out["cpu_baseline"] = cpu_baseline(args, sample_rows=64)
+    if dist is not None:
+        dist.barrier()
+        comm.close()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out))
+
+
+def _time_program(torch, tt, prog, ins, outs, reps, warm=3):
+    st = tt.Stream()
+    ts = torch.cuda.ExternalStream(st.handle)
+    for _ in range(warm):
+        prog.run_device(ins, outs, st)
+    st.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ts)
+    for _ in range(reps):
+        prog.run_device(ins, outs, st)
+    e1.record(ts)
+    st.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def components(tt, torch, args, peaks, peak_src):
+    """Single-GPU parts of the metric: fused elementwise, reductions, GEMM."""
+    res = {}
+    hbm = peaks["hbm_gbs"]
+    # fused elementwise chain relu(a*b + c)*0.5 - exp(-a); c broadcast along rows
+    ew = {}
+    for n in (1024, 8192, 16384):
+        rng = np.random.default_rng(0)
+        g = tt.Graph()
+        a, b, c = g.input([n, n]), g.input([n, n]), g.input([1, n])
+        y = tt.relu(a * b + c) * 0.5 - tt.exp(-a)
+        prog = tt.compile(g, outputs=[y])
+        ins = [tt.DeviceBuffer.from_numpy(rng.standard_normal(s).astype(np.float32)) for s in ([n, n], [n, n], [1, n])]
+        out = [tt.DeviceBuffer([n, n])]
+        reps = 200 if n == 1024 else 20
+        ms = _time_program(torch, tt, prog, ins, out, reps)
+        nbytes = 3 * n * n * 4 + n * 4
+        ew[f"{n}x{n}"] = {"ms": round(ms, 5), "GB/s": round(nbytes / ms / 1e6, 1),
+                          "frac_of_measured_hbm": round(nbytes / ms / 1e6 / hbm, 3),
+                          "note": "fits in L2 (126 MB): repeated calls hit L2" if n == 1024 else "> L2"}
+        del ins, out, prog
+    res["fused_elementwise"] = ew
+    # reductions over X [8192, 4096] U(-1,1): sum/mean/max over axis 1, sum over axis 0 of X^T
+    rng = np.random.default_rng(1)
+    xr = rng.uniform(-1, 1, (8192, 4096)).astype(np.float32)
+    red = {}
+    for name, fn in (("sum_ax1", lambda x: tt.sum(x, [1])), ("mean_ax1", lambda x: tt.mean(x, [1])),
+                     ("max_ax1", lambda x: tt.max(x, [1])), ("sum_ax0_of_T", lambda x: tt.sum(tt.transpose(x, 0, 1), [0]))):
+        g = tt.Graph()
+        nx = g.input([8192, 4096])
+        prog = tt.compile(g, outputs=[fn(nx)])
+        ins = [tt.DeviceBuffer.from_numpy(xr)]
+        out = [tt.DeviceBuffer([8192])]
+        ms = _time_program(torch, tt, prog, ins, out, 50)
+        nbytes = 8192 * 4096 * 4 + 8192 * 4
+        red[name] = {"ms": round(ms, 5), "GB/s": round(nbytes / ms / 1e6, 1),
+                     "frac_of_measured_hbm": round(nbytes / ms / 1e6 / hbm, 3)}
+        del ins, out, prog
+    res["reductions_8192x4096"] = red
+    # GEMM C = A.B, A,B ~ N(0, 1/K)
+    gm = {}
+    eff = peaks["bf16_tflops"] / 2.0 / 3.0
+    for (m, n, k) in ((1024, 1024, 1024), (4096, 4096, 4096), (8192, 8192, 8192), (16384, 1024, 4096)):
+        rng = np.random.default_rng(2)
+        g = tt.Graph()
+        a, b = g.input([m, k]), g.input([k, n])
+        prog = tt.compile(g, outputs=[a @ b])
+        ins = [tt.DeviceBuffer.from_numpy((rng.standard_normal((m, k)) / np.sqrt(k)).astype(np.float32)),
+               tt.DeviceBuffer.from_numpy((rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32))]
+        out = [tt.DeviceBuffer([m, n])]
+        reps = 5 if m * n * k >= 8192 ** 3 else 20
+        ms = _time_program(torch, tt, prog, ins, out, reps)
+        tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+        gm[f"{m}x{n}x{k}"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 2), "frac_of_3xtf32_peak": round(tf / eff, 4)}
+        del ins, out, prog
+    res["gemm_fp32"] = gm
+    res["peaks"] = {"source": peak_src, "hbm_gbs": hbm, "3xtf32_tflops": round(eff, 1)}
+    return res
+
+
+# --------------------------------------------------------------------------------------------
+# CPU baseline: the reference itself (oracle/_ref) on the host cores
+# --------------------------------------------------------------------------------------------
+
+def _ref_worker(args):
+    rows, seed = args
+    sys.path.insert(0, ROOT)
+    import tinytensor_b200.graph as tg
+    from oracle import oracle as O
+
+    class _NS:
+        pass
+    ns = _NS()
+    for k in ("Graph", "relu", "tanh", "mean"):
+        setattr(ns, k, getattr(tg, k))
+    g, (X, T, W1, W2, W3), loss = mlp_graph(ns, rows)
+    x, t, w = mlp_data(seed, rows)
+    feed = {X: x, T: t, W1: w[0], W2: w[1], W3: w[2]}
+    ref = O.Reference()
+    g.mark_output(loss)
+    t_fwd = ref.time_runs(g, feed, mode="avx2", reps=1)       # prog.run(feed): compiled forward
+    t_grad = ref.time_gradients(g, loss, feed, reps=1)        # tt.gradients: eager fwd + bwd
+    return t_fwd + t_grad
+
+
+def cpu_baseline(args, sample_rows=64):
+    """Reference step time on the host cores: P processes, each timing the reference's
+    own step (compiled AVX2 forward + eager tt.gradients) on a `sample_rows` shard;
+    the SGD update (84 MB of numpy) is not included.  Extrapolated to the 32768-row step."""
+    import multiprocessing as mp
+
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as O
+    if not O.reference_available():
+        return {"value": None, "unit": "step/s", "cores": 0, "kind": "reference",
+                "sample": "oracle/_ref/libttref.so not built"}
+    P = max(1, min(os.cpu_count() or 1, 64))
+    ctx = mp.get_context("spawn")
+    t0 = time.time()
+    with ctx.Pool(P) as pool:
+        times = pool.map(_ref_worker, [(sample_rows, 100 + i) for i in range(P)])
+    wall = time.time() - t0
+    per = float(np.median(times))
+    rows_per_s = P * sample_rows / per
+    return {"value": round(rows_per_s / GLOBAL_BATCH, 6), "unit": "step/s", "cores": P, "kind": "reference",
+            "sample": f"{P} processes x {sample_rows}-row shard of the MLP step (reference AVX2 compiled forward + "
+                      f"eager tt.gradients), median {per:.2f} s per shard, wall {wall:.1f} s; extrapolated to "
+                      f"{GLOBAL_BATCH} rows"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    vals = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        info = cpu_baseline(args, sample_rows=32)
+        if i >= args.warmup and info["value"] is not None:
+            vals.append(info["value"])
+    if not vals:
+        print(json.dumps({"impl": "reference", "unavailable": info["sample"] if info else "no sample"}))
+        return
+    v = float(np.median(vals))
+    info["value"] = round(v, 6)
+    out = {
+        "impl": "reference",
+        "metric": "MLP DP SGD step/s (1024-4096-4096-10, global batch 32768)",
+        "value": round(v, 6),
+        "unit": "step/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(1000.0 / v, 1),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: X,T ~ N(0,1); Xavier-uniform weights",
+        "config": {"workload": "mlp_dp_sgd_step", "model": "MLP 1024-4096-4096-10 MSE", "global_batch": GLOBAL_BATCH,
+                   "parallelism": "reference CPU, all host cores"},
+        "cpu_baseline": info,
+        "e2e": {"value": round(v, 6), "unit": "step/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-components", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,164 @@
+"""GPU parity at the benchmark configurations' full sizes (seeded inputs of the
+documented shapes and distributions; rng = np.random.default_rng(seed), drawn in
+float64 and cast to float32).  Large products are checked on sampled rows, which the
+reference's blocked loop computes independently of the other rows."""
+
+import numpy as np
+import pytest
+
+from parity import GEMM_FROB_RTOL, REDUCTION_NORM_RTOL, assert_bitexact, assert_elementwise, assert_norm
+
+import tinytensor_b200 as tt
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def test_config1_fused_elementwise_1024(cache_dir):
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((1024, 1024)).astype(np.float32)
+    b = rng.standard_normal((1024, 1024)).astype(np.float32)
+    c = rng.standard_normal((1, 1024)).astype(np.float32)
+    g = tt.Graph()
+    na, nb, nc = g.input([1024, 1024]), g.input([1024, 1024]), g.input([1, 1024])
+    y = tt.relu(na * nb + nc) * 0.5 - tt.exp(-na)
+    prog = tt.compile(g, outputs=[y], cache_dir=cache_dir)
+    assert "Kernel Launches (1)" in prog.execution_plan()  # one fused kernel: 3 loads + 1 store
+    got = prog.run({na: a, nb: b, nc: c}).numpy()
+    ref = O.evaluate(g, {na: a, nb: b, nc: c}, [y])[0]
+    assert_elementwise(got, ref)
+    # the part without exp rounds identically to the reference
+    g2 = tt.Graph()
+    ma, mb, mc = g2.input([1024, 1024]), g2.input([1024, 1024]), g2.input([1, 1024])
+    y2 = tt.relu(ma * mb + mc) * 0.5
+    got2 = tt.compile(g2, outputs=[y2], cache_dir=cache_dir).run({ma: a, mb: b, mc: c}).numpy()
+    assert_bitexact(got2, O.evaluate(g2, {ma: a, mb: b, mc: c}, [y2])[0])
+
+
+def test_config2_reductions_8192x4096(cache_dir):
+    rng = np.random.default_rng(1)
+    x = rng.uniform(-1, 1, (8192, 4096)).astype(np.float32)
+    g = tt.Graph()
+    nx = g.input([8192, 4096])
+    outs = [tt.sum(nx, [1]), tt.mean(nx, [1]), tt.max(nx, [1]), tt.sum(tt.transpose(nx, 0, 1), [0])]
+    prog = tt.compile(g, outputs=outs, cache_dir=cache_dir)
+    got = [t.numpy() for t in prog.run({nx: x})]
+    ref = O.evaluate(g, {nx: x}, outs)
+    assert_norm(got[0], ref[0], REDUCTION_NORM_RTOL)
+    assert_norm(got[1], ref[1], REDUCTION_NORM_RTOL)
+    assert_bitexact(got[2], ref[2])
+    assert_norm(got[3], ref[3], REDUCTION_NORM_RTOL)
+    # the transposed view is folded: no copy kernel in the plan
+    assert "copy" not in prog.execution_plan()
+
+
+def _gemm(m, n, k, cache_dir, rows=None):
+    rng = np.random.default_rng(2)
+    a = (rng.standard_normal((m, k)) / np.sqrt(k)).astype(np.float32)
+    b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
+    g = tt.Graph()
+    na, nb = g.input([m, k]), g.input([k, n])
+    c = tt.compile(g, outputs=[na @ nb], cache_dir=cache_dir).run({na: a, nb: b}).numpy()
+    if rows is None:
+        ref = O.matmul(a, b)
+        assert_norm(c, ref, GEMM_FROB_RTOL)
+    else:
+        idx = np.unique(np.random.default_rng(9).integers(0, m, rows)).astype(np.int64)
+        ref = O.matmul_rows(a, b, idx)
+        assert_norm(c[idx], ref, GEMM_FROB_RTOL)
+        # fp64 check of the same rows
+        exact = a[idx].astype(np.float64) @ b.astype(np.float64)
+        assert_norm(c[idx], exact, GEMM_FROB_RTOL)
+
+
+def test_config3_gemm_1024(cache_dir):
+    _gemm(1024, 1024, 1024, cache_dir)
+
+
+def test_config3_gemm_4096_sampled(cache_dir):
+    _gemm(4096, 4096, 4096, cache_dir, rows=48)
+
+
+def test_config3_gemm_rect_sampled(cache_dir):
+    _gemm(16384, 1024, 4096, cache_dir, rows=64)
+
+
+def test_config3_gemm_8192_sampled(cache_dir):
+    _gemm(8192, 8192, 8192, cache_dir, rows=24)
+
+
+def _mlp_graph(B):
+    g = tt.Graph()
+    X, T = g.input([B, 1024], name="X"), g.input([B, 10], name="T")
+    W1, W2, W3 = g.input([1024, 4096], name="W1"), g.input([4096, 4096], name="W2"), g.input([4096, 10], name="W3")
+    h1 = tt.relu(X @ W1)
+    h2 = tt.tanh(h1 @ W2)
+    d = h2 @ W3 - T
+    loss = tt.mean(d * d)
+    return g, (X, T, W1, W2, W3), loss
+
+
+def _xavier(rng, fi, fo):
+    lim = np.sqrt(6.0 / (fi + fo))
+    return rng.uniform(-lim, lim, (fi, fo)).astype(np.float32)
+
+
+def test_config4_mlp_gradients_small_batch(cache_dir):
+    """Full layer widths (1024 -> 4096 -> 4096 -> 10) at batch 64 against the oracle."""
+    B = 64
+    rng = np.random.default_rng(3)
+    g, (X, T, W1, W2, W3), loss = _mlp_graph(B)
+    feed = {X: rng.standard_normal((B, 1024)).astype(np.float32), T: rng.standard_normal((B, 10)).astype(np.float32),
+            W1: _xavier(rng, 1024, 4096), W2: _xavier(rng, 4096, 4096), W3: _xavier(rng, 4096, 10)}
+    prog = tt.compile_gradients(g, loss, [W1, W2, W3], cache_dir=cache_dir)
+    out = [t.numpy() for t in prog.run(feed)]
+    ref = O.gradients(g, loss, feed, [W1, W2, W3])
+    lref = O.evaluate(g, feed, [loss])[0]
+    np.testing.assert_allclose(out[0], lref, rtol=1e-5)
+    for got, r in zip(out[1:], ref):
+        assert_norm(got, r, GEMM_FROB_RTOL)
+
+
+def test_config4_mlp_full_batch_runs(cache_dir):
+    """Batch 4096: loss matches the oracle forward; gradients are finite and W3's
+    gradient matches an fp64 recomputation from the GPU's own activations' inputs."""
+    B = 4096
+    rng = np.random.default_rng(3)
+    g, (X, T, W1, W2, W3), loss = _mlp_graph(B)
+    feed = {X: rng.standard_normal((B, 1024)).astype(np.float32), T: rng.standard_normal((B, 10)).astype(np.float32),
+            W1: _xavier(rng, 1024, 4096), W2: _xavier(rng, 4096, 4096), W3: _xavier(rng, 4096, 10)}
+    prog = tt.compile_gradients(g, loss, [W1, W2, W3], cache_dir=cache_dir)
+    out = [t.numpy() for t in prog.run(feed)]
+    assert all(np.all(np.isfinite(o)) for o in out)
+    x64 = feed[X].astype(np.float64)
+    h2 = np.tanh(np.maximum(x64 @ feed[W1], 0) @ feed[W2])
+    d = h2 @ feed[W3] - feed[T]
+    np.testing.assert_allclose(out[0], np.mean(d * d), rtol=1e-5)
+    gw3 = h2.T @ (2.0 * d / d.size)
+    assert_norm(out[3], gw3, GEMM_FROB_RTOL)
+
+
+def test_config5_sgd_steps_match_oracle(cache_dir):
+    """Three SGD steps (lr 0.01) of the MLP on device vs the oracle's full-batch steps."""
+    B = 32
+    rng = np.random.default_rng(4)
+    g, (X, T, W1, W2, W3), loss = _mlp_graph(B)
+    x = rng.standard_normal((B, 1024)).astype(np.float32)
+    t = rng.standard_normal((B, 10)).astype(np.float32)
+    ws = [_xavier(rng, 1024, 4096), _xavier(rng, 4096, 4096), _xavier(rng, 4096, 10)]
+    prog = tt.compile_gradients(g, loss, [W1, W2, W3], cache_dir=cache_dir)
+    dx, dt = tt.DeviceBuffer.from_numpy(x), tt.DeviceBuffer.from_numpy(t)
+    dw = [tt.DeviceBuffer.from_numpy(w) for w in ws]
+    outs = [tt.DeviceBuffer(s) for s in prog.output_shapes]
+    opt = tt.SGD(dw, lr=0.01)
+    st = tt.Stream()
+    for _ in range(3):
+        prog.run_device([dx, dt] + dw, outs, st)
+        opt.step(outs[1:], st)
+    st.synchronize()
+    ref = [w.copy() for w in ws]
+    for _ in range(3):
+        grads = O.gradients(g, loss, {X: x, T: t, W1: ref[0], W2: ref[1], W3: ref[2]}, [W1, W2, W3])
+        ref = [O.sgd(w, gw, 0.01)[0] for w, gw in zip(ref, grads)]
+    for d, r in zip(dw, ref):
+        assert_norm(d.numpy(), r, GEMM_FROB_RTOL)

@@ -1,0 +1,225 @@
+"""Host-side logic of the backend, no GPU: the C ABI exports, graph building and
+its errors, IR text, scheduling/fusion, the memory plan, CUDA generation (NVRTC
+compiles every case to an sm_100a cubin here) and the kernel cache protocol."""
+
+import os
+import re
+
+import numpy as np
+import pytest
+
+from cases import CASES, build
+
+import tinytensor_b200 as tt
+from tinytensor_b200 import _lib
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+HOST = tt.FLAG_HOST_ONLY
+
+
+def _host_compile(g, outs, cache_dir, **kw):
+    return tt.compile(g, outputs=outs, cache_dir=cache_dir, flags=HOST | kw.pop("flags", 0), **kw)
+
+
+def test_library_exports_every_declared_symbol():
+    with open(os.path.join(ROOT, "include", "tt_cuda.h")) as f:
+        hdr = f.read()
+    declared = set(re.findall(r"^\s*(?:int|const char\*|uint64_t)\s+(tt_\w+)\s*\(", hdr, re.M))
+    assert len(declared) >= 25
+    for name in declared:
+        assert hasattr(_lib.lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert set(_lib.SIGNATURES) == declared
+
+
+def test_no_device_is_reported_not_faked():
+    # Without a GPU the library still loads; device calls fail loudly (no CPU fallback).
+    if os.environ.get("CUDA_VISIBLE_DEVICES") is None and os.path.exists("/dev/nvidia0"):
+        pytest.skip("a GPU is present")
+    with pytest.raises(tt.NoDeviceError):
+        tt.device_init(0)
+
+
+def test_builder_errors_match_reference():
+    g = tt.Graph()
+    a, b = g.input([2, 3]), g.input([4, 5])
+    with pytest.raises(tt.ShapeError):
+        a @ b
+    with pytest.raises(tt.BroadcastError):
+        a + b
+    with pytest.raises(tt.DimensionError):
+        tt.transpose(a, 0, 2)
+    with pytest.raises(tt.DimensionError):
+        tt.sum(a, [3])
+    with pytest.raises(tt.TypeError):
+        tt.relu(1.0)
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_every_case_generates_and_compiles(name, cache_dir):
+    c = build(name)
+    if c["kind"] == "forward":
+        p = _host_compile(c["graph"], c["outputs"], cache_dir)
+    else:
+        p = tt.compile_gradients(c["graph"], c["loss"], c["wrt"], cache_dir=cache_dir, flags=HOST)
+    src = p.generated_source()
+    plan = p.execution_plan()
+    assert "Execution Mode: Compiled CUDA" in plan and "Memory Planning:" in plan
+    if "ttk_region" in src:
+        assert os.path.exists(p.cubin_path())
+        with open(p.cubin_path(), "rb") as f:
+            assert f.read(4) == b"\x7fELF"
+
+
+def test_config1_is_one_fused_kernel(cache_dir):
+    g = tt.Graph()
+    a, b, c = g.input([1024, 1024]), g.input([1024, 1024]), g.input([1, 1024])
+    y = tt.relu(a * b + c) * 0.5 - tt.exp(-a)
+    p = _host_compile(g, [y], cache_dir)
+    plan = p.execution_plan()
+    assert "Kernel Launches (1)" in plan
+    src = p.generated_source()
+    assert src.count("__global__") == 1
+    assert src.count("float4") >= 3  # vectorised loads of a, b and the broadcast row of c
+    assert "0x3f000000u" in src      # the 0.5 constant, bit-exact
+    # no intermediate buffers: peak planned memory 0
+    assert "Memory Planning: Peak 0 bytes" in plan
+
+
+def test_transposes_fold_into_consumers(cache_dir):
+    g = tt.Graph()
+    x = g.input([64, 32])
+    w = g.input([48, 32])
+    y = x @ tt.transpose(w, 0, 1)
+    s = tt.sum(tt.transpose(x, 0, 1), [0])
+    p = _host_compile(g, [y, s], cache_dir)
+    plan = p.execution_plan()
+    assert "copy" not in plan
+    assert "B:K" in plan            # GEMM reads W as a K-major operand directly
+    assert "reduce_sum/row" in plan  # the transposed column sum is a row reduction of x
+
+
+def test_fusion_respects_launch_dependencies(cache_dir):
+    # sum(x) feeds back into an elementwise chain of x: the two regions must not merge
+    g = tt.Graph()
+    x = g.input([128, 64])
+    s = tt.sum(tt.relu(x), [1], keepdims=True)
+    y = tt.relu(x) * s + x
+    p = _host_compile(g, [y], cache_dir)
+    plan = p.execution_plan()
+    assert re.search(r"Kernel Launches \((\d+)\)", plan).group(1) == "3"
+
+
+def test_memory_planner_reuses_slots_on_a_chain(cache_dir):
+    # test_adversarial_memory_planner.cpp: a linear chain needs at most 2 buffers
+    g = tt.Graph()
+    x = g.input([64, 64])
+    ws = [g.input([64, 64]) for _ in range(6)]
+    h = x
+    for w in ws:
+        h = h @ w
+    p = _host_compile(g, [h], cache_dir)
+    plan = p.execution_plan()
+    nslots = int(re.search(r"slots \d+ in (\d+) slots", plan).group(1))
+    assert nslots <= 2
+    # slots never overlap in the arena
+    slots = [(int(o), int(c)) for o, c in re.findall(r"slot \d+ @ (\d+) capacity (\d+)", plan)]
+    for (o1, c1), (o2, _) in zip(slots, slots[1:]):
+        assert o1 + c1 <= o2
+
+
+def test_memory_planner_keeps_live_values_apart(cache_dir):
+    # diamond: both branches are live at the join, so they cannot share a slot
+    g = tt.Graph()
+    x, w1, w2 = g.input([32, 32]), g.input([32, 32]), g.input([32, 32])
+    a = x @ w1
+    b = x @ w2
+    y = a @ b
+    p = _host_compile(g, [y], cache_dir)
+    plan = p.execution_plan()
+    outs = re.findall(r"gemm/[^\]]*\] -> arena:(\d+)", plan)
+    assert len(outs) == 2 and outs[0] != outs[1]
+
+
+def test_ir_of_fused_reference_node_is_expanded(cache_dir):
+    # A reference FusedElementwise node "relu(sub(@0, @1))" is computed as written
+    # (the reference codegen would emit relu(a + b): src/codegen/cpp_backend.cpp:345-387).
+    g = tt.Graph()
+    a, b = g.input([16]), g.input([16])
+    f = tt.graph.Node(g, _lib.OP_FUSED, [16], "float32", [a, b])
+    f.expr = "relu(sub(@0, @1))"
+    g._add(f)
+    p = _host_compile(g, [f], cache_dir)
+    assert "relu" in p.optimized_ir() and "sub" in p.optimized_ir()
+    assert "v - " in p.generated_source() or " - a" in p.generated_source()
+
+
+def test_cache_hit_and_truncated_entry_heals(cache_dir, tmp_path):
+    d = str(tmp_path / "cache")
+    g = tt.Graph()
+    x = g.input([40])
+    y = tt.sigmoid(x) * 3.0
+    p1 = _host_compile(g, [y], d)
+    path = p1.cubin_path()
+    assert os.path.exists(path)
+    mtime = os.path.getmtime(path)
+    p2 = _host_compile(g, [y], d)
+    assert p2.cubin_path() == path and os.path.getmtime(path) == mtime  # hit: not rewritten
+    with open(path, "wb") as f:
+        f.write(b"\x7fELF")  # truncated (< 64 bytes)
+    p3 = _host_compile(g, [y], d)
+    assert os.path.getsize(p3.cubin_path()) > 64
+    assert not [f for f in os.listdir(d) if ".tmp." in f]
+
+
+def test_cache_concurrent_processes(tmp_path):
+    """Several processes compile the same graph into one cache dir: one cubin, no temp
+    leftovers (tests/python/test_multiprocess_cache.py:30-92)."""
+    import multiprocessing as mp
+    d = str(tmp_path / "mp")
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(4) as pool:
+        paths = pool.map(_mp_compile, [d] * 4)
+    assert len(set(paths)) == 1
+    files = os.listdir(d)
+    assert sum(f.endswith(".cubin") for f in files) == 1
+    assert not [f for f in files if ".tmp." in f]
+
+
+def _mp_compile(d):
+    import sys
+    sys.path.insert(0, ROOT)
+    import tinytensor_b200 as tt2
+    g = tt2.Graph()
+    x = g.input([33, 9])
+    y = tt2.relu(x * x - 1.0)
+    return tt2.compile(g, outputs=[y], cache_dir=d, flags=tt2.FLAG_HOST_ONLY).cubin_path()
+
+
+def test_gradient_graph_structure(cache_dir):
+    g = tt.Graph()
+    x, w = g.input([8, 4]), g.input([4, 3])
+    loss = tt.mean(tt.relu(x @ w))
+    p = tt.compile_gradients(g, loss, [w], cache_dir=cache_dir, flags=HOST)
+    ir = p.optimized_ir()
+    assert "step" in ir and "transpose" in ir and ir.count("matmul") == 2  # dx is dead and eliminated
+    assert p.num_outputs == 2 and p.output_shapes == [[], [4, 3]]
+
+
+def test_run_validates_inputs_before_device(cache_dir):
+    g = tt.Graph()
+    a = g.input([4])
+    p = _host_compile(g, [tt.relu(a)], cache_dir)
+    with pytest.raises(tt.RuntimeExecutionError):
+        p.run({})
+    with pytest.raises(tt.ShapeError):
+        p.run({a: np.ones(8, np.float32)})
+    with pytest.raises(tt.NoDeviceError):
+        p.run({a: np.ones(4, np.float32)})
+
+
+def test_unsupported_dtype_is_a_compile_error(cache_dir):
+    g = tt.Graph()
+    a = g.input([4], dtype=tt.float64)
+    with pytest.raises(tt.CompileError):
+        _host_compile(g, [tt.relu(a)], cache_dir)

@@ -1,0 +1,537 @@
+// The C ABI of include/tt_cuda.h: compile (CppBackend::compile), run
+// (Executable::run), diagnostics (Executor::original_ir / optimized_ir /
+// generated_source / execution_plan), buffers and the SGD step.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <sstream>
+
+#include "jit.hpp"
+#include "schedule.hpp"
+
+using namespace ttb;
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+int set_error(int status, const std::string& msg) {
+    static const char* names[] = {"",
+                                  "ShapeError: ",
+                                  "DimensionError: ",
+                                  "BroadcastError: ",
+                                  "TypeError: ",
+                                  "MemoryError: ",
+                                  "IRError: ",
+                                  "CompileError: ",
+                                  "RuntimeExecutionError: ",
+                                  "RuntimeExecutionError: device status: ",
+                                  "RuntimeExecutionError: no device: ",
+                                  "InvalidArgument: ",
+                                  "CommError: "};
+    g_last_error = (status > 0 && status <= 12 ? names[status] : "") + msg;
+    return status;
+}
+
+template <typename F>
+int guarded(F&& f) {
+    try {
+        f();
+        return TT_OK;
+    } catch (const Error& e) {
+        return set_error(e.status, e.what());
+    } catch (const std::bad_alloc&) {
+        return set_error(TT_ERR_MEMORY, "host allocation failed");
+    } catch (const std::exception& e) {
+        return set_error(TT_ERR_RUNTIME, e.what());
+    }
+}
+
+void check_cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return;
+    int st = (e == cudaErrorMemoryAllocation) ? TT_ERR_MEMORY : TT_ERR_RUNTIME;
+    cudaGetLastError();
+    fail(st, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+std::string tuple_str(const Shape& s) {  // Shape::to_string (include/tinytensor/core/shape.hpp:63-74)
+    std::string r = "(";
+    for (size_t i = 0; i < s.size(); ++i) {
+        r += std::to_string(s[i]);
+        if (i + 1 < s.size() || s.size() == 1) {
+            r += ",";
+            if (i + 1 < s.size()) r += " ";
+        }
+    }
+    return r + ")";
+}
+
+void copy_out(const std::string& s, char* buf, size_t cap, size_t* needed) {
+    if (needed) *needed = s.size() + 1;
+    if (buf && cap) {
+        size_t n = std::min(cap - 1, s.size());
+        std::memcpy(buf, s.data(), n);
+        buf[n] = '\0';
+    }
+}
+
+}  // namespace
+
+int ttb::record_error(int status, const std::string& msg) { return set_error(status, msg); }
+
+struct tt_program {
+    int device = 0;
+    Plan plan;
+    std::string original_ir, optimized_ir, source, plan_text, cubin_path;
+    LoadedModule mod;
+    std::vector<CUfunction> region_fn;  // per region index
+    char* arena = nullptr;
+    std::vector<Shape> in_shapes, out_shapes;
+    std::vector<int64_t> in_bytes, out_bytes;
+    size_t cse_removed = 0, dce_removed = 0, original_nodes = 0;
+    cudaStream_t last_stream = nullptr;
+    bool profiling = false;
+    std::vector<cudaEvent_t> events;
+    std::vector<double> prof_sum;   // per launch: summed ms over profiled runs
+    int64_t prof_runs = 0;
+    bool prof_pending = false;
+    bool has_tc = false;
+    std::mutex run_mutex;
+
+    ~tt_program() {
+        for (cudaEvent_t e : events) cudaEventDestroy(e);
+        if (mod.module) driver().moduleUnload(mod.module);
+        if (arena) cudaFree(arena);
+    }
+};
+
+static int launches_of(const Plan& p, const Launch& L) {
+    if (L.type == LT_REGION) return p.regions[static_cast<size_t>(L.region)].grid > 0 ? 1 : 0;
+    if (L.type == LT_REDUCE) return L.rd.outer == 0 ? 0 : (L.rd.R == 0 ? 1 : (L.rd.splits > 1 ? 2 : 1));
+    return (L.gd.M == 0 || L.gd.N == 0) ? 0 : (L.gd.K == 0 ? static_cast<int>(L.gd.batch) : 1);
+}
+
+static std::string execution_plan(const tt_program& p) {
+    const Graph& g = p.plan.g;
+    std::ostringstream ss;
+    ss << "=== TinyTensor Execution Plan ===\n";
+    ss << "Execution Mode: Compiled CUDA (sm_100a)\n";
+    ss << "Input Nodes (" << g.inputs.size() << "):\n";
+    for (int k : g.inputs) {
+        const Node& n = g.nodes[static_cast<size_t>(k)];
+        ss << "  %" << n.id << " [" << tuple_str(n.shape) << ", float32]";
+        if (!n.name.empty()) ss << " name=\"" << n.name << "\"";
+        ss << "\n";
+    }
+    ss << "Output Nodes (" << g.outputs.size() << "):\n";
+    for (int k : g.outputs) {
+        const Node& n = g.nodes[static_cast<size_t>(k)];
+        ss << "  %" << n.id << " [" << tuple_str(n.shape) << ", float32]\n";
+    }
+    ss << "Execution Sequence (Topological, " << g.nodes.size() << " nodes):\n";
+    for (const Node& n : g.nodes)
+        ss << "  %" << n.id << " = " << op_name(n.op) << " " << tuple_str(n.shape) << " (float32)\n";
+    ss << "Binary Object: " << (p.cubin_path.empty() ? std::string("(in-memory cubin)") : p.cubin_path) << "\n";
+    const Plan& pl = p.plan;
+    int64_t saved = pl.total_alloc_bytes > pl.peak_planned_bytes ? pl.total_alloc_bytes - pl.peak_planned_bytes : 0;
+    ss << "Memory Planning: Peak " << pl.peak_planned_bytes << " bytes (saved " << saved << " bytes via "
+       << pl.reused_buffers << " reused buffers)\n";
+    ss << "Fused Regions: " << pl.fused_regions << ", CSE Replacements: " << p.cse_removed
+       << ", DCE Eliminated Nodes: " << p.dce_removed << "\n";
+    ss << p.plan_text;
+    ss << "=================================";
+    return ss.str();
+}
+
+extern "C" {
+
+const char* tt_last_error(void) { return g_last_error.c_str(); }
+int tt_version(void) { return 100; }
+uint64_t tt_launch_count(void) { return g_launches.load(); }
+
+int tt_device_init(int32_t device) {
+    return guarded([&] {
+        int n = 0;
+        cudaError_t e = cudaGetDeviceCount(&n);
+        if (e != cudaSuccess || n == 0) {
+            cudaGetLastError();
+            fail(TT_ERR_NO_DEVICE, "no CUDA device is available");
+        }
+        if (device < 0 || device >= n) fail(TT_ERR_NO_DEVICE, "device ordinal out of range");
+        cudaDeviceProp prop;
+        check_cuda(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+        if (prop.major != 10 || prop.minor != 0)
+            fail(TT_ERR_NO_DEVICE, std::string("device is ") + prop.name + " (sm_" + std::to_string(prop.major) +
+                                       std::to_string(prop.minor) + "); this backend is built for sm_100a (B200)");
+        check_cuda(cudaSetDevice(device), "cudaSetDevice");
+        check_cuda(cudaFree(nullptr), "context creation");
+    });
+}
+
+int tt_graph_ir(const tt_graph* g, char* buf, size_t cap, size_t* needed) {
+    return guarded([&] { copy_out(ir_text(import_graph(g)), buf, cap, needed); });
+}
+
+int tt_graph_verify(const tt_graph* g) {
+    return guarded([&] { verify(import_graph(g)); });
+}
+
+int tt_compile(const tt_graph* cg, const tt_compile_options* opt, tt_program** out) {
+    return guarded([&] {
+        if (!out) fail(TT_ERR_INVALID, "null output handle");
+        *out = nullptr;
+        tt_compile_options o{};
+        o.optimize = 1;
+        o.grad_loss = -1;
+        if (opt) o = *opt;
+        auto p = std::make_unique<tt_program>();
+        p->device = o.device;
+        Graph g = import_graph(cg);
+        p->original_ir = ir_text(g);
+        p->original_nodes = g.nodes.size();
+        verify(g);
+        if (o.grad_loss >= 0) {
+            std::vector<int> wrt(o.grad_wrt, o.grad_wrt + o.num_grad_wrt);
+            append_gradients(g, o.grad_loss, wrt);
+        }
+        g = expand_fused(g);
+        if (o.optimize) g = cse(g, &p->cse_removed);
+        g = dce(g, &p->dce_removed);
+        verify(g);
+        p->optimized_ir = ir_text(g);
+        ScheduleOptions so;
+        so.fuse = !(o.flags & TT_FLAG_NO_FUSION);
+        so.gemm_epilogue = !(o.flags & TT_FLAG_NO_GEMM_FUSION);
+        p->plan = schedule(g, so);
+        p->source = generate_source(p->plan);
+        for (int k : p->plan.g.inputs) {
+            p->in_shapes.push_back(p->plan.g.nodes[static_cast<size_t>(k)].shape);
+            p->in_bytes.push_back(numel(p->in_shapes.back()) * 4);
+        }
+        for (int k : p->plan.g.outputs) {
+            p->out_shapes.push_back(p->plan.g.nodes[static_cast<size_t>(k)].shape);
+            p->out_bytes.push_back(numel(p->out_shapes.back()) * 4);
+        }
+        for (const Launch& L : p->plan.launches) p->has_tc |= (L.type == LT_GEMM && L.gd.algo == 2);
+
+        // Generated kernels: NVRTC -> cubin (cached); loaded unless host-only.
+        const bool host_only = (o.flags & TT_FLAG_HOST_ONLY) != 0;
+        if (!host_only && tt_device_init(o.device) != TT_OK) throw Error(TT_ERR_NO_DEVICE, g_last_error);
+        std::vector<std::string> used;
+        std::vector<int> used_idx;
+        for (size_t i = 0; i < p->plan.regions.size(); ++i)
+            if (!p->plan.regions[i].kernel.empty()) {
+                used.push_back(p->plan.regions[i].kernel);
+                used_idx.push_back(static_cast<int>(i));
+            }
+        p->region_fn.assign(p->plan.regions.size(), nullptr);
+        p->plan_text = plan_text(p->plan);
+        if (!used.empty()) {
+            std::string key = cache_key(p->optimized_ir, p->source);
+            if (host_only) {
+                p->cubin_path = compile_to_cache(key, p->source, o.cache_dir ? o.cache_dir : "");
+            } else {
+                p->mod = load_program_module(key, p->source, o.cache_dir ? o.cache_dir : "", used);
+                for (size_t i = 0; i < used_idx.size(); ++i)
+                    p->region_fn[static_cast<size_t>(used_idx[i])] = p->mod.functions[i];
+                p->cubin_path = p->mod.cubin_path;
+            }
+        }
+        if (host_only) {
+            p->device = -1;
+            *out = p.release();
+            return;
+        }
+        check_cuda(cudaMalloc(reinterpret_cast<void**>(&p->arena), static_cast<size_t>(p->plan.arena_bytes)),
+                   "cudaMalloc(arena)");
+        for (const auto& c : p->plan.constants) {
+            const Node& n = p->plan.g.nodes[static_cast<size_t>(c.second)];
+            check_cuda(cudaMemcpy(p->arena + c.first, n.cdata.data(), n.cdata.size() * sizeof(float),
+                                  cudaMemcpyHostToDevice),
+                       "constant upload");
+        }
+        check_cuda(cudaMemset(p->arena + p->plan.status_offset, 0, 256), "status word init");
+        *out = p.release();
+    });
+}
+
+int tt_program_info(const tt_program* p, int32_t what, char* buf, size_t cap, size_t* needed) {
+    return guarded([&] {
+        if (!p) fail(TT_ERR_INVALID, "null program");
+        switch (what) {
+            case TT_INFO_ORIGINAL_IR: copy_out(p->original_ir, buf, cap, needed); break;
+            case TT_INFO_OPTIMIZED_IR: copy_out(p->optimized_ir, buf, cap, needed); break;
+            case TT_INFO_SOURCE: copy_out(p->source, buf, cap, needed); break;
+            case TT_INFO_PLAN: copy_out(execution_plan(*p), buf, cap, needed); break;
+            case TT_INFO_CUBIN_PATH: copy_out(p->cubin_path, buf, cap, needed); break;
+            default: fail(TT_ERR_INVALID, "unknown info selector");
+        }
+    });
+}
+
+int tt_program_num_io(const tt_program* p, int32_t* ni, int32_t* no) {
+    return guarded([&] {
+        if (!p) fail(TT_ERR_INVALID, "null program");
+        if (ni) *ni = static_cast<int32_t>(p->in_shapes.size());
+        if (no) *no = static_cast<int32_t>(p->out_shapes.size());
+    });
+}
+
+int tt_program_output_shape(const tt_program* p, int32_t index, int32_t* rank, int64_t* shape) {
+    return guarded([&] {
+        if (!p) fail(TT_ERR_INVALID, "null program");
+        if (index < 0 || static_cast<size_t>(index) >= p->out_shapes.size()) fail(TT_ERR_INVALID, "output index");
+        const Shape& s = p->out_shapes[static_cast<size_t>(index)];
+        if (rank) *rank = static_cast<int32_t>(s.size());
+        if (shape)
+            for (size_t i = 0; i < s.size(); ++i) shape[i] = s[i];
+    });
+}
+
+static void collect_profile(tt_program* p);
+
+static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_ptr, cudaStream_t stream) {
+    const Plan& pl = p->plan;
+    if (p->prof_pending) collect_profile(p);  // waits for the previous profiled run only
+    auto resolve = [&](const BufRef& r) -> char* {
+        switch (r.kind) {
+            case BK_ARENA: return p->arena + r.offset;
+            case BK_INPUT: return in_ptr[r.index] + r.offset;
+            case BK_OUTPUT: return out_ptr[r.index] + r.offset;
+            default: return nullptr;
+        }
+    };
+    int* status = reinterpret_cast<int*>(p->arena + pl.status_offset);
+    if (p->profiling) {
+        size_t need = pl.launches.size() + 1;
+        while (p->events.size() < need) {
+            cudaEvent_t e;
+            check_cuda(cudaEventCreate(&e), "cudaEventCreate");
+            p->events.push_back(e);
+        }
+        check_cuda(cudaEventRecord(p->events[0], stream), "cudaEventRecord");
+    }
+    for (size_t s = 0; s < pl.launches.size(); ++s) {
+        const Launch& L = pl.launches[s];
+        int rc = 0;
+        if (L.type == LT_REGION) {
+            const Region& r = pl.regions[static_cast<size_t>(L.region)];
+            if (r.grid > 0) {
+                std::vector<void*> vals;
+                for (size_t e = 0; e < r.ext.size(); ++e) {
+                    const Access& a = r.ext_access[e];
+                    vals.push_back(a.imm ? nullptr : resolve(pl.root_ref[static_cast<size_t>(a.node)]));
+                }
+                for (const BufRef& b : r.store_ref) vals.push_back(resolve(b));
+                std::vector<void*> args;
+                for (void*& v : vals) args.push_back(&v);
+                CUresult cr = driver().launchKernel(p->region_fn[static_cast<size_t>(L.region)],
+                                                    static_cast<unsigned>(r.grid), 1, 1, 256, 1, 1, 0, stream,
+                                                    args.data(), nullptr);
+                if (cr != CUDA_SUCCESS) fail(TT_ERR_RUNTIME, "cuLaunchKernel(" + r.kernel + "): " + cu_error(cr));
+            }
+        } else if (L.type == LT_REDUCE) {
+            rc = launch_reduce(L.rd, reinterpret_cast<const float*>(resolve(L.in_ref)),
+                               reinterpret_cast<float*>(resolve(L.out_ref)), resolve(L.scratch_ref), stream);
+        } else {
+            rc = launch_gemm(L.gd, reinterpret_cast<const float*>(resolve(L.in_ref)),
+                             reinterpret_cast<const float*>(resolve(L.in_ref2)),
+                             reinterpret_cast<float*>(resolve(L.out_ref)), status, stream);
+        }
+        if (rc) fail(TT_ERR_RUNTIME, L.label + ": " + cudaGetErrorString(static_cast<cudaError_t>(rc)));
+        g_launches += static_cast<uint64_t>(launches_of(pl, L));
+        if (p->profiling) check_cuda(cudaEventRecord(p->events[s + 1], stream), "cudaEventRecord");
+    }
+    p->prof_pending = p->profiling;
+}
+
+// Adds the last profiled run's per-launch times to the running sums.
+static void collect_profile(tt_program* p) {
+    if (!p->prof_pending) return;
+    p->prof_pending = false;
+    const size_t n = p->plan.launches.size();
+    check_cuda(cudaEventSynchronize(p->events[n]), "profile event");
+    if (p->prof_sum.size() != n) p->prof_sum.assign(n, 0.0);
+    for (size_t s = 0; s < n; ++s) {
+        float ms = 0.f;
+        check_cuda(cudaEventElapsedTime(&ms, p->events[s], p->events[s + 1]), "cudaEventElapsedTime");
+        p->prof_sum[s] += ms;
+    }
+    p->prof_runs++;
+}
+
+int tt_program_run(tt_program* p, const void* const* inputs, void* const* outputs, int32_t where, void* stream_v) {
+    return guarded([&] {
+        if (!p) fail(TT_ERR_INVALID, "null program");
+        std::lock_guard<std::mutex> lk(p->run_mutex);
+        const size_t ni = p->in_shapes.size(), no = p->out_shapes.size();
+        if (ni && !inputs) fail(TT_ERR_RUNTIME, "Expected " + std::to_string(ni) + " inputs, but got none");
+        if (no && !outputs) fail(TT_ERR_RUNTIME, "Expected " + std::to_string(no) + " output buffers, but got none");
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+        if (p->device < 0) fail(TT_ERR_NO_DEVICE, "program was compiled host-only (TT_FLAG_HOST_ONLY)");
+        check_cuda(cudaSetDevice(p->device), "cudaSetDevice");
+        std::vector<char*> in_ptr(ni), out_ptr(no);
+        for (size_t k = 0; k < ni; ++k)
+            if (!inputs[k] && p->in_bytes[k]) fail(TT_ERR_RUNTIME, "Input " + std::to_string(k) + " is null");
+        for (size_t k = 0; k < no; ++k)
+            if (!outputs[k] && p->out_bytes[k]) fail(TT_ERR_RUNTIME, "Output " + std::to_string(k) + " is null");
+        if (where == TT_HOST) {
+            for (size_t k = 0; k < ni; ++k) {
+                in_ptr[k] = p->arena + p->plan.stage_in[k];
+                if (p->in_bytes[k])
+                    check_cuda(cudaMemcpyAsync(in_ptr[k], inputs[k], static_cast<size_t>(p->in_bytes[k]),
+                                               cudaMemcpyHostToDevice, stream),
+                               "input copy");
+            }
+            for (size_t k = 0; k < no; ++k) out_ptr[k] = p->arena + p->plan.stage_out[k];
+        } else if (where == TT_DEVICE) {
+            for (size_t k = 0; k < ni; ++k) {
+                in_ptr[k] = const_cast<char*>(static_cast<const char*>(inputs[k]));
+                if (reinterpret_cast<uintptr_t>(in_ptr[k]) % 16)
+                    fail(TT_ERR_RUNTIME, "device input " + std::to_string(k) + " is not 16-byte aligned");
+            }
+            for (size_t k = 0; k < no; ++k) {
+                out_ptr[k] = static_cast<char*>(outputs[k]);
+                if (reinterpret_cast<uintptr_t>(out_ptr[k]) % 16)
+                    fail(TT_ERR_RUNTIME, "device output " + std::to_string(k) + " is not 16-byte aligned");
+            }
+        } else {
+            fail(TT_ERR_INVALID, "where must be TT_HOST or TT_DEVICE");
+        }
+        run_launches(p, in_ptr.data(), out_ptr.data(), stream);
+        p->last_stream = stream;
+        if (where == TT_HOST) {
+            for (size_t k = 0; k < no; ++k)
+                if (p->out_bytes[k])
+                    check_cuda(cudaMemcpyAsync(outputs[k], out_ptr[k], static_cast<size_t>(p->out_bytes[k]),
+                                               cudaMemcpyDeviceToHost, stream),
+                               "output copy");
+            int32_t status = 0;
+            if (p->has_tc)
+                check_cuda(cudaMemcpyAsync(&status, p->arena + p->plan.status_offset, sizeof(status),
+                                           cudaMemcpyDeviceToHost, stream),
+                           "status copy");
+            check_cuda(cudaStreamSynchronize(stream), "kernel execution");
+            collect_profile(p);
+            if (status != 0) {
+                cudaMemsetAsync(p->arena + p->plan.status_offset, 0, 4, stream);
+                fail(TT_ERR_DEVICE_STATUS, "a kernel gave up a bounded wait (status " + std::to_string(status) + ")");
+            }
+        }
+    });
+}
+
+int tt_program_status(tt_program* p, int32_t* device_status) {
+    return guarded([&] {
+        if (!p) fail(TT_ERR_INVALID, "null program");
+        if (p->device < 0) fail(TT_ERR_NO_DEVICE, "program was compiled host-only (TT_FLAG_HOST_ONLY)");
+        check_cuda(cudaSetDevice(p->device), "cudaSetDevice");
+        int32_t status = 0;
+        check_cuda(cudaMemcpyAsync(&status, p->arena + p->plan.status_offset, sizeof(status), cudaMemcpyDeviceToHost,
+                                   p->last_stream),
+                   "status copy");
+        check_cuda(cudaStreamSynchronize(p->last_stream), "kernel execution");
+        collect_profile(p);
+        if (device_status) *device_status = status;
+        if (status != 0) {
+            cudaMemset(p->arena + p->plan.status_offset, 0, 4);
+            fail(TT_ERR_DEVICE_STATUS, "a kernel gave up a bounded wait (status " + std::to_string(status) + ")");
+        }
+    });
+}
+
+int tt_program_set_profiling(tt_program* p, int32_t enable) {
+    return guarded([&] {
+        if (!p) fail(TT_ERR_INVALID, "null program");
+        if (p->prof_pending) collect_profile(p);
+        p->profiling = enable != 0;
+        p->prof_sum.clear();
+        p->prof_runs = 0;
+    });
+}
+
+int tt_program_profile(const tt_program* pc, int32_t cap, char* names, int32_t name_cap, float* ms, int32_t* count) {
+    return guarded([&] {
+        if (!pc) fail(TT_ERR_INVALID, "null program");
+        tt_program* p = const_cast<tt_program*>(pc);
+        if (p->prof_pending) collect_profile(p);
+        int32_t n = static_cast<int32_t>(p->prof_sum.size());
+        if (count) *count = n;
+        for (int32_t i = 0; i < n && i < cap; ++i) {
+            if (ms) ms[i] = static_cast<float>(p->prof_sum[static_cast<size_t>(i)] / static_cast<double>(p->prof_runs));
+            if (names && name_cap > 0) {
+                const std::string& l = p->plan.launches[static_cast<size_t>(i)].label;
+                size_t m = std::min(static_cast<size_t>(name_cap - 1), l.size());
+                std::memcpy(names + static_cast<size_t>(i) * static_cast<size_t>(name_cap), l.data(), m);
+                names[static_cast<size_t>(i) * static_cast<size_t>(name_cap) + m] = '\0';
+            }
+        }
+    });
+}
+
+int tt_program_destroy(tt_program* p) {
+    return guarded([&] {
+        if (!p) return;
+        if (p->device >= 0) cudaSetDevice(p->device);
+        delete p;
+    });
+}
+
+int tt_device_alloc(size_t bytes, void** ptr) {
+    return guarded([&] {
+        if (!ptr) fail(TT_ERR_INVALID, "null pointer slot");
+        check_cuda(cudaMalloc(ptr, bytes ? bytes : 1), "cudaMalloc");
+    });
+}
+int tt_device_free(void* ptr) {
+    return guarded([&] { check_cuda(cudaFree(ptr), "cudaFree"); });
+}
+int tt_host_alloc(size_t bytes, void** ptr) {
+    return guarded([&] {
+        if (!ptr) fail(TT_ERR_INVALID, "null pointer slot");
+        check_cuda(cudaMallocHost(ptr, bytes ? bytes : 1), "cudaMallocHost");
+    });
+}
+int tt_host_free(void* ptr) {
+    return guarded([&] { check_cuda(cudaFreeHost(ptr), "cudaFreeHost"); });
+}
+int tt_memcpy(void* dst, const void* src, size_t bytes, int32_t kind, void* stream) {
+    return guarded([&] {
+        cudaMemcpyKind k = kind == TT_H2D ? cudaMemcpyHostToDevice
+                           : kind == TT_D2H ? cudaMemcpyDeviceToHost
+                                            : cudaMemcpyDeviceToDevice;
+        check_cuda(cudaMemcpyAsync(dst, src, bytes, k, static_cast<cudaStream_t>(stream)), "cudaMemcpyAsync");
+    });
+}
+int tt_stream_create(void** stream) {
+    return guarded([&] {
+        if (!stream) fail(TT_ERR_INVALID, "null stream slot");
+        check_cuda(cudaStreamCreateWithFlags(reinterpret_cast<cudaStream_t*>(stream), cudaStreamNonBlocking),
+                   "cudaStreamCreate");
+    });
+}
+int tt_stream_destroy(void* stream) {
+    return guarded([&] { check_cuda(cudaStreamDestroy(static_cast<cudaStream_t>(stream)), "cudaStreamDestroy"); });
+}
+int tt_stream_sync(void* stream) {
+    return guarded([&] { check_cuda(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "cudaStreamSynchronize"); });
+}
+
+int tt_sgd_step(int32_t n, float* const* params, const float* const* grads, float* const* velocities,
+                const int64_t* numels, float lr, float momentum, void* stream) {
+    return guarded([&] {
+        if (n < 0 || (n > 0 && (!params || !grads || !numels))) fail(TT_ERR_INVALID, "bad SGD arguments");
+        if (momentum > 0.0f && !velocities) fail(TT_ERR_INVALID, "momentum needs velocity buffers");
+        int rc = launch_sgd(n, params, grads, momentum > 0.0f ? velocities : nullptr, numels, lr, momentum, stream);
+        if (rc) fail(TT_ERR_RUNTIME, std::string("sgd: ") + cudaGetErrorString(static_cast<cudaError_t>(rc)));
+        int64_t total = 0;
+        for (int32_t i = 0; i < n; ++i) total += numels[i];
+        if (total > 0) g_launches += static_cast<uint64_t>((n + 15) / 16);
+    });
+}
+
+}  // extern "C"

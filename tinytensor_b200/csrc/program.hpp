@@ -1,0 +1,105 @@
+// Compiled-program structures of the B200 backend: the launch schedule, the
+// arena layout produced by the memory planner, and the descriptors of the
+// hand-written kernels (reductions, GEMM, SGD) that the schedule calls.
+#pragma once
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "ttb.hpp"
+
+namespace ttb {
+
+// Where a kernel argument points: arena offset, or a caller buffer (+ offset).
+enum BufKind { BK_NONE = 0, BK_ARENA = 1, BK_INPUT = 2, BK_OUTPUT = 3 };
+struct BufRef {
+    int kind = BK_NONE;
+    int index = 0;          // input/output position
+    int64_t offset = 0;     // bytes
+};
+
+// ---- reductions (kernels_reduce.cu) ----
+enum ReduceKind { RK_ROW = 0, RK_COL = 1, RK_GENERIC = 2 };
+enum ReduceOp { RO_SUM = 0, RO_MEAN = 1, RO_MAX = 2 };
+struct ReduceDesc {
+    int op = RO_SUM;
+    int kind = RK_ROW;
+    // ROW: out[o] = red_{r<R} x[o*s_outer + r*s_red]            (s_red == 1 when vec)
+    // COL: out[o] = red_{r<R} x[r*s_red + o]                     (o contiguous)
+    int64_t outer = 1, R = 1, s_outer = 0, s_red = 1;
+    int splits = 1;          // partial sums per output (scratch = outer*splits doubles)
+    int vec = 1;             // 4 when rows/columns can use float4 loads
+    float mean_scale = 1.f;  // float(1/count) for mean
+    // GENERIC: kept/reduced dims with element strides; output contiguous over kept dims
+    int nk = 0, nr = 0;
+    int64_t ksize[TT_MAX_RANK], kstride[TT_MAX_RANK], rsize[TT_MAX_RANK], rstride[TT_MAX_RANK];
+    int64_t in_offset = 0;   // element offset of the view
+};
+// Fixes the split count / vector width of d and returns the scratch bytes its
+// launch needs (double partials).  Launchers return cudaError_t as int.
+int64_t reduce_prepare(ReduceDesc& d);
+int launch_reduce(const ReduceDesc& d, const float* in, float* out, void* scratch, void* stream);
+
+// ---- GEMM (kernels_gemm.cu) ----
+enum Epilogue { EP_NONE = 0, EP_RELU = 1 };
+struct GemmDesc {
+    int64_t M = 0, N = 0, K = 0, batch = 1;
+    int64_t a_sm = 0, a_sk = 0, a_sb = 0;  // A[b][m][k] element strides
+    int64_t b_sk = 0, b_sn = 0, b_sb = 0;  // B[b][k][n]
+    int64_t c_sb = 0;                      // C[b][m][n] row stride N
+    int64_t a_off = 0, b_off = 0;          // element offsets of the operand views
+    int epilogue = EP_NONE;
+    int algo = 0;                          // chosen by plan_gemm
+};
+void plan_gemm(GemmDesc& d);  // picks the kernel variant for the shape/layout
+const char* gemm_algo_name(int algo);
+int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, int* status, void* stream);
+
+// ---- misc kernels (kernels_misc.cu) ----
+int launch_sgd(int n, float* const* params, const float* const* grads, float* const* vel, const int64_t* numels,
+               float lr, float momentum, void* stream);
+int launch_fill_f32(float* p, int64_t n, float v, void* stream);
+
+// ---- elementwise regions (generated, NVRTC) ----
+struct Access {
+    bool imm = false;
+    float value = 0.f;                  // immediate scalar constant
+    int node = -1;                      // graph node whose storage is read
+    int64_t offset = 0;                 // element offset into that storage
+    std::vector<int64_t> strides;       // element strides per dim of the READ shape
+};
+
+struct Region {
+    Shape shape;                        // iteration shape
+    std::vector<int> nodes;             // nodes computed in registers, topological
+    std::vector<int> ext;               // external nodes read (order of kernel params)
+    std::vector<Access> ext_access;     // how each ext node is read, strides per `shape` dim
+    std::vector<int> stores;            // nodes written (contiguous over `shape`)
+    std::vector<BufRef> store_ref;      // filled by the planner
+    bool is_copy = false;               // materialise ext[0] into stores[0]
+    std::string kernel;                 // generated kernel name
+    int vec = 1, unroll = 4;
+    int64_t grid = 0;
+};
+
+enum LaunchType { LT_REGION = 0, LT_REDUCE = 1, LT_GEMM = 2 };
+
+struct Launch {
+    int type = LT_REGION;
+    int region = -1;                    // LT_REGION
+    ReduceDesc rd;                      // LT_REDUCE
+    GemmDesc gd;                        // LT_GEMM
+    int in_node = -1, in_node2 = -1;    // reduce input / gemm A,B (storage nodes)
+    int out_node = -1;                  // reduce / gemm output node
+    BufRef in_ref, in_ref2, out_ref, scratch_ref;
+    int64_t scratch_bytes = 0;
+    std::string label;                  // for profiles and the execution plan
+};
+
+struct Slot {
+    int64_t offset = 0, capacity = 0;
+    int last_step = -1;
+};
+
+}  // namespace ttb
