@@ -213,6 +213,62 @@ def evaluate(graph, feed, outputs=None):
     return [vals[o.index] for o in outs]
 
 
+def magnitude(graph, feed, outputs=None):
+    """Per-element magnitude bound m(x) of each output, in float64: the expression
+    evaluated with |.| on every operand and + for every + or -, so that the rounding
+    error of any float32 evaluation order is O(u * m).  Used as the scale of the
+    elementwise tolerance for expressions with transcendental functions, whose float
+    libm results (glibc vs CUDA) may differ by an ulp before a cancelling subtraction."""
+    vals, mags = {}, {}
+    for n in graph.nodes:
+        if n.op == INPUT:
+            v = np.asarray(feed[n], dtype=np.float64).reshape(n.shape)
+            vals[n.index], mags[n.index] = v, np.abs(v)
+            continue
+        if n.op == CONSTANT:
+            v = np.asarray(n.data, dtype=np.float64)
+            vals[n.index], mags[n.index] = v, np.abs(v)
+            continue
+        x = [vals[q.index] for q in n.inputs]
+        m = [mags[q.index] for q in n.inputs]
+        op = n.op
+        with np.errstate(all="ignore"):
+            if op in (ADD, SUB):
+                v, mg = (x[0] + x[1]) if op == ADD else (x[0] - x[1]), m[0] + m[1]
+            elif op == MUL:
+                v, mg = x[0] * x[1], m[0] * m[1]
+            elif op == DIV:
+                v, mg = x[0] / x[1], m[0] / np.abs(x[1])
+            elif op == RELU:
+                v = np.where(x[0] > 0, x[0], 0.0)
+                mg = np.where(x[0] > 0, m[0], 0.0)
+            elif op == STEP:
+                v = np.where(x[0] > 0, 1.0, 0.0)
+                mg = v
+            elif op == NEG:
+                v, mg = -x[0], m[0]
+            elif op == EXP:
+                v = np.exp(x[0])
+                mg = v * (1.0 + m[0])
+            elif op == TANH:
+                v = np.tanh(x[0])
+                mg = np.abs(v) + m[0] * (1.0 - v * v)
+            elif op == SIGMOID:
+                v = 1.0 / (1.0 + np.exp(-x[0]))
+                mg = v + m[0] * v * (1.0 - v)
+            elif op == TRANSPOSE:
+                v, mg = np.swapaxes(x[0], n.dim0, n.dim1), np.swapaxes(m[0], n.dim0, n.dim1)
+            elif op == RESHAPE:
+                v, mg = x[0].reshape(n.shape), m[0].reshape(n.shape)
+            elif op == EXPAND:
+                v, mg = np.broadcast_to(x[0], n.shape), np.broadcast_to(m[0], n.shape)
+            else:
+                raise ValueError(f"magnitude: unsupported op {op}")
+        vals[n.index], mags[n.index] = v, mg
+    outs = graph.outputs if outputs is None else outputs
+    return [mags[o.index] for o in outs]
+
+
 def unbroadcast(g, target):
     """Autodiff::unbroadcast (gradient.cpp:10-50)."""
     target = tuple(target)

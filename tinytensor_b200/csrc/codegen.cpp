@@ -172,8 +172,8 @@ static void emit_region(std::ostringstream& ss, const Plan& p, Region& r) {
             case TT_OP_RELU: ss << "(" << x << " > 0.0f) ? " << x << " : 0.0f"; break;
             case TT_OP_STEP: ss << "(" << x << " > 0.0f) ? 1.0f : 0.0f"; break;
             case TT_OP_NEG: ss << "-" << x; break;
-            case TT_OP_EXP: ss << "expf(" << x << ")"; break;
-            case TT_OP_TANH: ss << "tanhf(" << x << ")"; break;
+            case TT_OP_EXP: ss << "tt_exp(" << x << ")"; break;
+            case TT_OP_TANH: ss << "tt_tanh(" << x << ")"; break;
             case TT_OP_SIGMOID:
                 ss << "tt_sigmoid(" << x << ")";
                 break;
@@ -205,10 +205,15 @@ std::string generate_source(Plan& p) {
         std::string line;
         while (std::getline(ir, line)) ss << "//   " << line << "\n";
     }
-    ss << "\n// Two-branch stable sigmoid, src/core/operators.cpp:211-232.\n";
+    ss << "\n// exp and tanh are evaluated in double and rounded once to float, which gives\n"
+          "// the correctly rounded float result except in vanishingly rare double-rounding\n"
+          "// cases (more accurate than a float libm such as the reference's std::exp).\n";
+    ss << "__device__ __forceinline__ float tt_exp(float x) { return (float)exp((double)x); }\n";
+    ss << "__device__ __forceinline__ float tt_tanh(float x) { return (float)tanh((double)x); }\n";
+    ss << "// Two-branch stable sigmoid in float, src/core/operators.cpp:211-232.\n";
     ss << "__device__ __forceinline__ float tt_sigmoid(float x) {\n"
-          "  if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));\n"
-          "  const float ex = expf(x);\n"
+          "  if (x >= 0.0f) return 1.0f / (1.0f + tt_exp(-x));\n"
+          "  const float ex = tt_exp(x);\n"
           "  return ex / (1.0f + ex);\n"
           "}\n\n";
     for (Launch& L : p.launches)

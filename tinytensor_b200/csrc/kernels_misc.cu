@@ -31,13 +31,14 @@ __global__ void __launch_bounds__(256) sgd_kernel(SgdArgs a) {
         int t = 0;
         while (i >= a.start[t + 1]) ++t;
         const int64_t j = i - a.start[t];
+        // explicitly rounded multiply and add/sub (no FMA contraction), as numpy rounds them
         float u = a.g[t][j];
         if (a.momentum > 0.0f) {
-            const float nv = a.momentum * a.v[t][j] + u;
+            const float nv = __fadd_rn(__fmul_rn(a.momentum, a.v[t][j]), u);
             a.v[t][j] = nv;
             u = nv;
         }
-        a.p[t][j] = a.p[t][j] - a.lr * u;
+        a.p[t][j] = __fsub_rn(a.p[t][j], __fmul_rn(a.lr, u));
     }
 }
 

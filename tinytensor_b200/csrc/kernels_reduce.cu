@@ -206,7 +206,7 @@ __global__ void fill_kernel(float* p, int64_t n, float v) {
 constexpr int64_t kTargetWarps = 148 * 64;
 
 int row_splits(int64_t outer, int64_t R) {
-    if (outer >= kTargetWarps / 2) return 1;
+    if (outer <= 0 || outer >= kTargetWarps / 2) return 1;
     int64_t s = (kTargetWarps + outer - 1) / outer;
     int64_t maxs = R / 1024;  // keep >= 1024 elements per warp
     if (s > maxs) s = maxs;
@@ -216,6 +216,7 @@ int row_splits(int64_t outer, int64_t R) {
 }
 
 int col_splits(int64_t outer, int64_t R, int vec) {
+    if (outer <= 0) return 1;
     int64_t threads = (outer + vec - 1) / vec;
     int64_t target = 148 * 2048;
     if (threads >= target / 2) return 1;
