@@ -89,6 +89,22 @@ def test_config3_gemm_8192_sampled(cache_dir):
     _gemm(8192, 8192, 8192, cache_dir, rows=24)
 
 
+def test_gemm_long_k_split_and_tails(cache_dir):
+    """K = 32768 (TMEM chunking + split-K), N not a multiple of the tile, transposed A."""
+    rng = np.random.default_rng(12)
+    m, n, k = 520, 300, 32768
+    at = (rng.standard_normal((k, m)) / np.sqrt(k)).astype(np.float32)  # A = at^T, an M-major view
+    b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
+    g = tt.Graph()
+    nat, nb = g.input([k, m]), g.input([k, n])
+    prog = tt.compile(g, outputs=[tt.transpose(nat, 0, 1) @ nb], cache_dir=cache_dir)
+    assert "tcgen05" in prog.execution_plan() and "splitk" in prog.execution_plan()
+    c = prog.run({nat: at, nb: b}).numpy()
+    idx = np.arange(0, m, 13, dtype=np.int64)
+    assert_norm(c[idx], O.matmul_rows(at.T, b, idx), GEMM_FROB_RTOL)
+    assert_norm(c[idx], at.T[idx].astype(np.float64) @ b.astype(np.float64), GEMM_FROB_RTOL)
+
+
 def _mlp_graph(B):
     g = tt.Graph()
     X, T = g.input([B, 1024], name="X"), g.input([B, 10], name="T")

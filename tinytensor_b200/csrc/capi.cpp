@@ -112,7 +112,7 @@ struct tt_program {
 static int launches_of(const Plan& p, const Launch& L) {
     if (L.type == LT_REGION) return p.regions[static_cast<size_t>(L.region)].grid > 0 ? 1 : 0;
     if (L.type == LT_REDUCE) return L.rd.outer == 0 ? 0 : (L.rd.R == 0 ? 1 : (L.rd.splits > 1 ? 2 : 1));
-    return (L.gd.M == 0 || L.gd.N == 0) ? 0 : (L.gd.K == 0 ? static_cast<int>(L.gd.batch) : 1);
+    return gemm_launch_count(L.gd);
 }
 
 static std::string execution_plan(const tt_program& p) {
@@ -340,7 +340,7 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
         } else {
             rc = launch_gemm(L.gd, reinterpret_cast<const float*>(resolve(L.in_ref)),
                              reinterpret_cast<const float*>(resolve(L.in_ref2)),
-                             reinterpret_cast<float*>(resolve(L.out_ref)), status, stream);
+                             reinterpret_cast<float*>(resolve(L.out_ref)), resolve(L.scratch_ref), status, stream);
         }
         if (rc) fail(TT_ERR_RUNTIME, L.label + ": " + cudaGetErrorString(static_cast<cudaError_t>(rc)));
         g_launches += static_cast<uint64_t>(launches_of(pl, L));

@@ -16,8 +16,12 @@
 
 namespace ttb {
 
-int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, int* status, void* stream);
+int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
+                   void* stream);
 bool gemm_tc_supported(const GemmDesc& d);
+int64_t gemm_tc_scratch_bytes(const GemmDesc& d);
+int gemm_tc_launch_count(const GemmDesc& d);
+void gemm_tc_plan(GemmDesc& d);
 
 namespace {
 
@@ -183,7 +187,10 @@ void plan_gemm(GemmDesc& d) {
         d.b_sk = 1;
     }
     if (d.N == 1) d.b_sn = 1;
-    if (gemm_tc_supported(d)) d.algo = ALGO_TC;
+    if (gemm_tc_supported(d)) {
+        d.algo = ALGO_TC;
+        gemm_tc_plan(d);
+    }
     else if (d.N <= 16) d.algo = ALGO_NARROW;
     else d.algo = ALGO_SIMT;
 }
@@ -196,7 +203,16 @@ const char* gemm_algo_name(int algo) {
     }
 }
 
-int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, int* status, void* stream) {
+int64_t gemm_scratch_bytes(const GemmDesc& d) { return d.algo == ALGO_TC ? gemm_tc_scratch_bytes(d) : 0; }
+
+int gemm_launch_count(const GemmDesc& d) {
+    if (d.M == 0 || d.N == 0 || d.batch == 0) return 0;
+    if (d.K == 0) return static_cast<int>(d.batch);
+    return d.algo == ALGO_TC ? gemm_tc_launch_count(d) : 1;
+}
+
+int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
+                void* stream) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (d.M == 0 || d.N == 0 || d.batch == 0) return 0;
     A += d.a_off;
@@ -209,7 +225,7 @@ int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, int
         }
         return 0;
     }
-    if (d.algo == ALGO_TC) return launch_gemm_tc(d, A, B, C, status, stream);
+    if (d.algo == ALGO_TC) return launch_gemm_tc(d, A, B, C, scratch, status, stream);
     if (d.algo == ALGO_NARROW) {
         dim3 grid(static_cast<unsigned>((d.M + 255) / 256), static_cast<unsigned>((d.N + 15) / 16),
                   static_cast<unsigned>(d.batch));

@@ -1,14 +1,532 @@
-// tcgen05 / TMEM 3xTF32 GEMM for sm_100a (placeholder until the tensor-core kernel lands).
+// fp32-accurate GEMM on the 5th-generation tensor cores (sm_100a): 3xTF32.
+//
+// Each fp32 operand x is split once into hi = tf32_rna(x) (low 13 mantissa bits zero,
+// so the tensor core uses it exactly) and lo = x - hi (exact in fp32; the tensor core
+// keeps its top 11 significant bits).  C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi; the dropped
+// A_lo.B_lo term and the truncation of lo are O(2^-21) relative.
+//
+// Accumulation: the tensor core's fp32 accumulation does not round to nearest (its
+// error grows with the number of accumulation steps; measured ~7e-9 * K relative on
+// B200), so TMEM only accumulates CHUNKS of `chunk_kb` 32-wide K blocks (256 values of
+// K by default).  Two TMEM accumulators (2 x 256 columns) alternate: while the MMA
+// issuer fills one chunk, eight epilogue warps drain the previous one into fp32
+// registers with round-to-nearest adds.  With 256-wide chunks the product meets the
+// 1e-5 relative-Frobenius contract against the reference's fp32 matmul
+// (src/core/operators.cpp:235-319) at any K.
+//
+// Pipeline (one 128x256 output tile per CTA, 320 threads):
+//   split pre-pass : K-major hi/lo copies of both operands in scratch (M/N-major views
+//                    transposed through shared memory), K padded to 4 floats so rows
+//                    are 16-byte aligned for TMA;
+//   warp 0         : TMA producer, 2 stages x (A_hi, A_lo, B_hi, B_lo) 128-B swizzled
+//                    tiles of 32 floats along K, completion on mbarriers;
+//   warp 1         : allocates 512 TMEM columns; one elected thread issues
+//                    tcgen05.mma.kind::tf32 (M=128, N=256, K=8; 3 products per step);
+//                    tcgen05.commit frees smem stages and publishes finished chunks;
+//   warps 2..9     : drain chunks (tcgen05.ld 32 lanes x 32 columns), keep the row's
+//                    128 columns in registers, store to C (or to a split-K partial).
+// Split-K (ksplit > 1, for grids smaller than the GPU): CTA z handles a contiguous
+// range of K blocks and writes a partial tile; a reduce kernel sums the partials in
+// split order (deterministic) and applies the epilogue.
+// No TMA multicast: every CTA loads its own tiles (the kernel also runs inside
+// multi-GPU jobs).  Every mbarrier wait is bounded by a clock budget; on expiry the
+// kernel records a code in the program's status word, raises a CTA-wide abort flag
+// (other CTAs see the status word and stop too), waits (bounded) for its own copies
+// in flight, frees its TMEM and returns.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdint>
+#include <mutex>
+
+#include "jit.hpp"
 #include "program.hpp"
 
 namespace ttb {
 
-bool gemm_tc_supported(const GemmDesc&) { return false; }
+namespace {
 
-int launch_gemm_tc(const GemmDesc&, const float*, const float*, float*, int*, void*) {
-    return static_cast<int>(cudaErrorNotSupported);
+constexpr int BM = 128, BN = 256, BK = 32, STAGES = 2;
+constexpr int A_TILE = BM * BK * 4;                    // 16 KB
+constexpr int B_TILE = BN * BK * 4;                    // 32 KB
+constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;   // 96 KB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 2048;
+constexpr uint32_t TMEM_COLS = 512;                    // two 256-column accumulators
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;           // 320
+constexpr long long WAIT_BUDGET = 4000000000LL;        // ~2 s of SM clock
+
+enum : int { ST_TIMEOUT_EMPTY = 0x100, ST_TIMEOUT_FULL = 0x200, ST_TIMEOUT_TFULL = 0x300, ST_TIMEOUT_TEMPTY = 0x400 };
+
+struct TcParams {
+    float* C;            // output, or the split-K partial buffer
+    int64_t ldc, c_bstride;
+    int M, N, K;
+    int a_batched, b_batched;
+    int ksplit, kb_per_split, chunk_kb;
+    int epilogue;        // applied here only when ksplit == 1
+    int* status;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: false if the phase does not complete within the clock budget, if this
+// CTA has aborted, or if another CTA has already reported a timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                          int code) {
+    const long long t0 = clock64();
+    uint32_t polls = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if ((++polls & 255u) == 0 && *reinterpret_cast<volatile int*>(status) != 0) {
+            *abort_flag = 1;
+            return false;
+        }
+        if (clock64() - t0 > WAIT_BUDGET) {
+            *abort_flag = 1;
+            atomicCAS(status, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of 128 B,
+// 8-row swizzle atoms 1024 B apart (SBO); LBO is unused for swizzled K-major layouts.
+__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(1u) << 16;             // LBO = 16 B
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;     // SBO = 1024 B
+    d |= static_cast<uint64_t>(1u) << 46;             // descriptor version (sm_100)
+    d |= static_cast<uint64_t>(2u) << 61;             // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                            (static_cast<uint32_t>(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+                   const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo, TcParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* tiles = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;   // [2] chunk accumulated  (MMA -> epilogue)
+    uint64_t* tempty = tfull + 2;       // [2] chunk drained      (epilogue -> MMA)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int zb_all = blockIdx.z;
+    const int batch = zb_all / p.ksplit, split = zb_all - batch * p.ksplit;
+    const int za = p.a_batched ? batch : 0, zb = p.b_batched ? batch : 0;
+    const int nkb_total = (p.K + BK - 1) / BK;
+    const int kb0 = split * p.kb_per_split;
+    const int kcount = max(0, min(nkb_total, kb0 + p.kb_per_split) - kb0);
+    const int nchunks = (kcount + p.chunk_kb - 1) / p.chunk_kb;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], EPI_WARPS);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_ahi)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_bhi)) : "memory");
+            int issued = 0;
+            for (int i = 0; i < kcount; ++i) {
+                const int s = i % STAGES;
+                const uint32_t ph = (i / STAGES) & 1;
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ST_TIMEOUT_EMPTY)) break;
+                uint8_t* st = tiles + s * STAGE_BYTES;
+                const int kx = (kb0 + i) * BK;
+                mbar_expect_tx(&full[s], STAGE_BYTES);
+                tma_load_3d(st, &tm_ahi, &full[s], kx, m0, za);
+                tma_load_3d(st + A_TILE, &tm_alo, &full[s], kx, m0, za);
+                tma_load_3d(st + 2 * A_TILE, &tm_bhi, &full[s], kx, n0, zb);
+                tma_load_3d(st + 2 * A_TILE + B_TILE, &tm_blo, &full[s], kx, n0, zb);
+                issued = i + 1;
+            }
+            if (*abort_flag) {
+                // let the copies already issued land before this CTA's shared memory goes away
+                for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i) {
+                    const long long t0 = clock64();
+                    while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) && clock64() - t0 < WAIT_BUDGET) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int i = 0; i < kcount; ++i) {
+                const int s = i % STAGES;
+                const uint32_t ph = (i / STAGES) & 1;
+                const int c = i / p.chunk_kb, within = i - c * p.chunk_kb;
+                const int b = c & 1;
+                if (within == 0) {
+                    if (!mbar_wait(&tempty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.status, ST_TIMEOUT_TEMPTY)) break;
+                }
+                if (!mbar_wait(&full[s], ph, abort_flag, p.status, ST_TIMEOUT_FULL)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t acc = tmem + static_cast<uint32_t>(b * 256);
+                const uint32_t st = smem_u32(tiles + s * STAGE_BYTES);
+                const uint32_t ahi = st, alo = st + A_TILE, bhi = st + 2 * A_TILE, blo = st + 2 * A_TILE + B_TILE;
+#pragma unroll
+                for (int k = 0; k < BK / 8; ++k) {
+                    const uint32_t off = k * 32;  // 8 tf32 = 32 B along the swizzled 128-B row
+                    const uint64_t dah = desc_kmajor_sw128(ahi + off), dal = desc_kmajor_sw128(alo + off);
+                    const uint64_t dbh = desc_kmajor_sw128(bhi + off), dbl = desc_kmajor_sw128(blo + off);
+                    mma_tf32(acc, dah, dbh, (within | k) != 0);
+                    mma_tf32(acc, dah, dbl, 1u);
+                    mma_tf32(acc, dal, dbh, 1u);
+                }
+                mma_commit(&empty[s]);
+                if (within == p.chunk_kb - 1 || i == kcount - 1) mma_commit(&tfull[b]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // epilogue warp e (0..7): TMEM lanes 32*(warp%4).., columns 128*(e/4) .. +127
+        const int e = warp - 2, q = warp & 3, h = e >> 2;
+        const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+        float acc[128];
+#pragma unroll
+        for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+        bool ok = true;
+        for (int c = 0; c < nchunks; ++c) {
+            const int b = c & 1;
+            ok = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (c >> 1) & 1, abort_flag, p.status, ST_TIMEOUT_TFULL));
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t r[32];
+                tmem_ld32(tmem + lane_base + static_cast<uint32_t>(b * 256 + h * 128 + j * 32), r);
+#pragma unroll
+                for (int t = 0; t < 32; ++t) acc[j * 32 + t] = __fadd_rn(acc[j * 32 + t], __uint_as_float(r[t]));
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+        }
+        if (ok) {
+            const int row = m0 + q * 32 + lane;
+            float* crow = p.C + static_cast<int64_t>(zb_all) * p.c_bstride + static_cast<int64_t>(row) * p.ldc;
+            const bool vec_ok = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                                (p.c_bstride % 4 == 0);
+            if (row < p.M) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int col0 = n0 + h * 128 + j * 32;
+                    if (col0 >= p.N) break;
+                    float v[32];
+#pragma unroll
+                    for (int t = 0; t < 32; ++t) {
+                        v[t] = acc[j * 32 + t];
+                        if (p.epilogue == EP_RELU) v[t] = v[t] > 0.0f ? v[t] : 0.0f;
+                    }
+                    if (vec_ok && col0 + 32 <= p.N) {
+#pragma unroll
+                        for (int t = 0; t < 32; t += 4)
+                            *reinterpret_cast<float4*>(crow + col0 + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
+                    } else {
+#pragma unroll
+                        for (int t = 0; t < 32; ++t)
+                            if (col0 + t < p.N) crow[col0 + t] = v[t];
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
+// Sums split-K partials P[b][s][i] in split order and applies the epilogue.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ P, float* __restrict__ C,
+                                                            int64_t per, int ksplit, int64_t c_bstride, int epilogue) {
+    const int64_t b = blockIdx.y;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < per;
+         i += static_cast<int64_t>(gridDim.x) * 256) {
+        float v = 0.0f;
+        for (int s = 0; s < ksplit; ++s) v = __fadd_rn(v, __ldg(P + (b * ksplit + s) * per + i));
+        if (epilogue == EP_RELU) v = v > 0.0f ? v : 0.0f;
+        C[b * c_bstride + i] = v;
+    }
+}
+
+// ---- split pre-pass: X (rows R along M or N, K columns, any strides) -> hi/lo [b][R][Kp] ----
+__device__ __forceinline__ void split_one(float x, float& hi, float& lo) {
+    uint32_t h;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+    hi = __uint_as_float(h);
+    lo = isfinite(x) ? __fsub_rn(x, hi) : 0.0f;
+}
+
+// K contiguous (or general strides): one thread per element, k fastest.
+__global__ void __launch_bounds__(256) split_rowmajor_kernel(const float* __restrict__ X, float* __restrict__ hi,
+                                                             float* __restrict__ lo, int64_t R, int64_t K, int64_t Kp,
+                                                             int64_t s_r, int64_t s_k, int64_t s_b) {
+    const int64_t per = R * K;
+    const int64_t b = blockIdx.y;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < per;
+         i += static_cast<int64_t>(gridDim.x) * 256) {
+        const int64_t r = i / K, k = i - r * K;
+        float h, l;
+        split_one(__ldg(X + b * s_b + r * s_r + k * s_k), h, l);
+        const int64_t o = (b * R + r) * Kp + k;
+        hi[o] = h;
+        lo[o] = l;
+    }
+}
+
+// R contiguous (an M- or N-major view): 32x32 tiles transposed through shared memory.
+__global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ X, float* __restrict__ hi,
+                                                              float* __restrict__ lo, int64_t R, int64_t K, int64_t Kp,
+                                                              int64_t s_k, int64_t s_b) {
+    __shared__ float th[32][33], tl[32][33];
+    const int64_t b = blockIdx.z;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 32, k0 = static_cast<int64_t>(blockIdx.y) * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+    for (int j = ty; j < 32; j += 8) {
+        const int64_t r = r0 + tx, k = k0 + j;
+        float h = 0.f, l = 0.f;
+        if (r < R && k < K) split_one(__ldg(X + b * s_b + k * s_k + r), h, l);
+        th[j][tx] = h;
+        tl[j][tx] = l;
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += 8) {
+        const int64_t r = r0 + j, k = k0 + tx;
+        if (r < R && k < K) {
+            const int64_t o = (b * R + r) * Kp + k;
+            hi[o] = th[tx][j];
+            lo[o] = tl[tx][j];
+        }
+    }
+}
+
+int launch_split(const float* X, float* hi, float* lo, int64_t R, int64_t K, int64_t Kp, int64_t s_r, int64_t s_k,
+                 int64_t s_b, int64_t nb, cudaStream_t st) {
+    if (R == 0 || K == 0) return 0;
+    if (s_r == 1 && s_k != 1) {
+        dim3 grid(static_cast<unsigned>((R + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(nb));
+        split_transpose_kernel<<<grid, 256, 0, st>>>(X, hi, lo, R, K, Kp, s_k, s_b);
+    } else {
+        int64_t blocks = (R * K + 255) / 256;
+        if (blocks > 148 * 32) blocks = 148 * 32;
+        dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(nb));
+        split_rowmajor_kernel<<<grid, 256, 0, st>>>(X, hi, lo, R, K, Kp, s_r, s_k, s_b);
+    }
+    return static_cast<int>(cudaGetLastError());
+}
+
+int64_t round4(int64_t x) { return (x + 3) / 4 * 4; }
+int64_t align256b(int64_t bytes) { return (bytes + 255) / 256 * 256; }
+
+void encode_kmajor(CUtensorMap* map, const float* base, int64_t K, int64_t Kp, int64_t rows, int64_t nb, int box_rows) {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(nb)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(Kp * 4), static_cast<cuuint64_t>(rows * Kp * 4)};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = driver().tensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
+                                               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(TT_ERR_RUNTIME, "cuTensorMapEncodeTiled: " + cu_error(r));
+}
+
+int64_t tiles_of(const GemmDesc& d) { return ((d.M + BM - 1) / BM) * ((d.N + BN - 1) / BN) * d.batch; }
+
+}  // namespace
+
+bool gemm_tc_supported(const GemmDesc& d) {
+    const bool big = d.M >= 64 && (d.N >= 64 || d.K >= 512);
+    return big && d.K >= 1 && d.batch <= 65535 && d.M < (1LL << 31) && d.N < (1LL << 31) && d.K < (1LL << 31);
+}
+
+// Split-K so that small tile grids still cover the GPU; each split keeps >= 16 K blocks.
+void gemm_tc_plan(GemmDesc& d) {
+    const int64_t nkb = (d.K + BK - 1) / BK;
+    const int64_t tiles = tiles_of(d);
+    int64_t ks = 1;
+    if (tiles < 120) {
+        ks = (148 + tiles - 1) / tiles;
+        const int64_t cap = nkb / 16;
+        if (ks > cap) ks = cap;
+        if (ks < 1) ks = 1;
+        if (ks * d.batch > 65535) ks = 65535 / d.batch;
+    }
+    const int64_t per = (nkb + ks - 1) / ks;
+    d.ksplit = static_cast<int>((nkb + per - 1) / per);  // every split has >= 1 K block
+}
+
+int64_t gemm_tc_scratch_bytes(const GemmDesc& d) {
+    const int64_t Kp = round4(d.K);
+    const int64_t ba = d.a_sb ? d.batch : 1, bb = d.b_sb ? d.batch : 1;
+    int64_t bytes = 2 * align256b(ba * d.M * Kp * 4) + 2 * align256b(bb * d.N * Kp * 4);
+    if (d.ksplit > 1) bytes += align256b(d.batch * d.ksplit * d.M * d.N * 4);
+    return bytes;
+}
+
+int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
+                   void* stream) {
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    static std::once_flag attr_once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once, [] {
+        attr_err = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    });
+    if (attr_err != cudaSuccess) return static_cast<int>(attr_err);
+    const int64_t Kp = round4(d.K);
+    const int64_t ba = d.a_sb ? d.batch : 1, bb = d.b_sb ? d.batch : 1;
+    char* s = static_cast<char*>(scratch);
+    float* ahi = reinterpret_cast<float*>(s);
+    s += align256b(ba * d.M * Kp * 4);
+    float* alo = reinterpret_cast<float*>(s);
+    s += align256b(ba * d.M * Kp * 4);
+    float* bhi = reinterpret_cast<float*>(s);
+    s += align256b(bb * d.N * Kp * 4);
+    float* blo = reinterpret_cast<float*>(s);
+    s += align256b(bb * d.N * Kp * 4);
+    float* partial = reinterpret_cast<float*>(s);
+    int rc = launch_split(A, ahi, alo, d.M, d.K, Kp, d.a_sm, d.a_sk, d.a_sb, ba, st);
+    if (rc) return rc;
+    rc = launch_split(B, bhi, blo, d.N, d.K, Kp, d.b_sn, d.b_sk, d.b_sb, bb, st);
+    if (rc) return rc;
+    CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+    encode_kmajor(&m_ahi, ahi, d.K, Kp, d.M, ba, BM);
+    encode_kmajor(&m_alo, alo, d.K, Kp, d.M, ba, BM);
+    encode_kmajor(&m_bhi, bhi, d.K, Kp, d.N, bb, BN);
+    encode_kmajor(&m_blo, blo, d.K, Kp, d.N, bb, BN);
+    const int64_t nkb = (d.K + BK - 1) / BK;
+    TcParams p;
+    p.M = static_cast<int>(d.M);
+    p.N = static_cast<int>(d.N);
+    p.K = static_cast<int>(d.K);
+    p.a_batched = d.a_sb != 0;
+    p.b_batched = d.b_sb != 0;
+    p.ksplit = d.ksplit;
+    p.kb_per_split = static_cast<int>((nkb + d.ksplit - 1) / d.ksplit);
+    p.chunk_kb = d.chunk_kb > 0 ? d.chunk_kb : 8;
+    p.status = status;
+    if (d.ksplit > 1) {
+        p.C = partial;
+        p.ldc = d.N;
+        p.c_bstride = d.M * d.N;  // partial index (batch * ksplit + split)
+        p.epilogue = EP_NONE;
+    } else {
+        p.C = C;
+        p.ldc = d.N;
+        p.c_bstride = d.c_sb;
+        p.epilogue = d.epilogue;
+    }
+    dim3 grid(static_cast<unsigned>((d.N + BN - 1) / BN), static_cast<unsigned>((d.M + BM - 1) / BM),
+              static_cast<unsigned>(d.batch * d.ksplit));
+    gemm_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(m_ahi, m_alo, m_bhi, m_blo, p);
+    rc = static_cast<int>(cudaGetLastError());
+    if (rc || d.ksplit == 1) return rc;
+    const int64_t per = d.M * d.N;
+    int64_t blocks = (per + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    splitk_reduce_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(d.batch)), 256, 0, st>>>(
+        partial, C, per, d.ksplit, d.c_sb, d.epilogue);
+    return static_cast<int>(cudaGetLastError());
+}
+
+int gemm_tc_launch_count(const GemmDesc& d) {
+    int n = 1;
+    if (d.M && d.K) ++n;
+    if (d.N && d.K) ++n;
+    if (d.ksplit > 1) ++n;
+    return n;
 }
 
 }  // namespace ttb

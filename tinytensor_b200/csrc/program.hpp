@@ -51,10 +51,15 @@ struct GemmDesc {
     int64_t a_off = 0, b_off = 0;          // element offsets of the operand views
     int epilogue = EP_NONE;
     int algo = 0;                          // chosen by plan_gemm
+    int ksplit = 1;                        // tensor-core kernel: K split across CTAs
+    int chunk_kb = 8;                      // tensor-core kernel: 32-wide K blocks per TMEM chunk
 };
 void plan_gemm(GemmDesc& d);  // picks the kernel variant for the shape/layout
 const char* gemm_algo_name(int algo);
-int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, int* status, void* stream);
+int64_t gemm_scratch_bytes(const GemmDesc& d);  // device scratch the chosen variant needs
+int gemm_launch_count(const GemmDesc& d);        // kernels one launch_gemm issues
+int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
+                void* stream);
 
 // ---- misc kernels (kernels_misc.cu) ----
 int launch_sgd(int n, float* const* params, const float* const* grads, float* const* vel, const int64_t* numels,

@@ -590,9 +590,11 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
             d.c_sb = d.M * d.N;
             if (d.M == 1) d.a_sm = d.a_sk == 1 ? d.K : 1;
             plan_gemm(d);
+            L.scratch_bytes = gemm_scratch_bytes(d);
             std::ostringstream lb;
             lb << "gemm/" << gemm_algo_name(d.algo) << "[" << d.M << "x" << d.N << "x" << d.K;
             if (d.batch > 1) lb << " b" << d.batch;
+            if (d.ksplit > 1) lb << " splitk" << d.ksplit;
             lb << (d.a_sk == 1 ? " A:K" : " A:M") << (d.b_sn == 1 ? " B:N" : " B:K") << "]";
             L.label = lb.str();
         }
