@@ -197,6 +197,19 @@ int tt_stream_sync(void* stream);
 int tt_sgd_step(int32_t n, float* const* params, const float* const* grads, float* const* velocities,
                 const int64_t* numels, float lr, float momentum, void* stream);
 
+/* ---- fp32-accurate GEMM that allocates nothing (no counterpart in the reference) ----
+ * C[M,N] = A[M,K] . B[K,N], row-major contiguous float32 device arrays, queued on
+ * `stream`, same kernels and accuracy as a compiled matmul.  For callers that cannot
+ * call cudaMalloc: its scratch is a static device array of 32 MiB per GPU that loads
+ * the library (held until exit); products needing more are rejected with
+ * TT_ERR_MEMORY.  The first call on a device resolves the array's address
+ * (cudaGetSymbolAddress) and should come before any stream capture.  All calls share
+ * the array: calls that overlap on the GPU race, so order them on one stream.
+ * device_status: optional device int the kernels set if a bounded wait gives up
+ * (caller clears it); NULL uses an internal word. */
+int tt_gemm_f32_noalloc(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                        int32_t* device_status, void* stream);
+
 /* ---- data parallel: NCCL over NVLink (no reference counterpart) ---- */
 typedef struct tt_dp tt_dp;
 #define TT_DP_ID_BYTES 128

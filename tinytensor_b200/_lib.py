@@ -170,6 +170,7 @@ SIGNATURES = {
         ctypes.c_int,
         [_I32, ctypes.POINTER(_VP), ctypes.POINTER(_VP), ctypes.POINTER(_VP), ctypes.POINTER(_I64), _F, _F, _VP],
     ),
+    "tt_gemm_f32_noalloc": (ctypes.c_int, [_VP, _VP, _VP, _I64, _I64, _I64, _VP, _VP]),
     "tt_dp_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
     "tt_dp_init": (ctypes.c_int, [_I32, _I32, ctypes.c_char_p, _I32, ctypes.POINTER(_VP)]),
     "tt_dp_allreduce_sum": (ctypes.c_int, [_VP, _VP, _SZ, _VP]),
