@@ -39,6 +39,20 @@ def load_peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
+def load_traffic(label):
+    """DRAM bytes per launch measured by ncu for `label` (profiles/traffic_per_launch.txt,
+    lines '<launch label> <bytes> <how>'), or None."""
+    p = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            parts = line.strip().split()
+            if len(parts) >= 2 and not line.startswith("#") and label.startswith(parts[0]):
+                return int(float(parts[1]))
+    return None
+
+
 def mlp_flops(rows, with_dx=False):
     fwd = 2 * rows * (1024 * 4096 + 4096 * 4096 + 4096 * 10)
     bwd = 2 * fwd if with_dx else 2 * fwd - 2 * rows * 1024 * 4096
@@ -239,10 +253,14 @@ def run_b200(args):
         "peak": round(eff_peak, 1),
         "unit": "TFLOP/s",
         "frac": round(gemm_flops / (top_ms * 1e-3) / 1e12 / eff_peak, 4) if gemm_flops else None,
-        "traffic": None,
+        "traffic": load_traffic(top_lbl),
         "peak_source": f"{peak_src}: bf16_tflops/2 (TF32) /3 (3xTF32 products), fp32-equivalent",
         "avg_ms": round(top_ms, 4),
+        "timed": "CUDA events on the launch stream around the GEMM launch (its hi/lo split pre-pass included)",
     }
+    total_prof = sum(t for _, t in prof)
+    step_profile = [{"launch": lbl, "ms": round(t, 4), "share": round(t / total_prof, 4)}
+                    for lbl, t in sorted(prof, key=lambda p: -p[1])[:10]]
     step_flops = mlp_flops(GLOBAL_BATCH)
     out = {
         "metric": "MLP DP SGD step/s (1024-4096-4096-10, global batch 32768)",
@@ -266,6 +284,7 @@ def run_b200(args):
                 "h2d_bytes_per_step": int(dx.nbytes + dt.nbytes) * world, "d2h_bytes_per_step": 4 * world},
         "gpu_launches": int(launches),
         "roofline": roofline,
+        "step_profile": step_profile,
         "clocks": clk,
     }
     if world == 1 and not args.no_components:
@@ -450,13 +469,56 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-components", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="mlp", choices=["mlp", "gemm", "elementwise", "reduce"],
+                    help="mlp: the headline step; the others time one compiled program (profiling cases)")
+    ap.add_argument("--size", default=None, help="gemm: M,N,K; elementwise: n (an n x n chain); reduce: R,C")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "mlp":
+        run_single(args)
     else:
         run_b200(args)
+
+
+def run_single(args):
+    """One compiled program of a single-GPU component, timed with CUDA events over
+    `steps` runs on device-resident inputs (inputs > L2 for the default sizes)."""
+    import torch
+
+    import tinytensor_b200 as tt
+
+    tt.device_init(0)
+    rng = np.random.default_rng(0)
+    g = tt.Graph()
+    if args.workload == "gemm":
+        m, n, k = (int(v) for v in (args.size or "4096,4096,4096").split(","))
+        a, b = g.input([m, k]), g.input([k, n])
+        outs = [a @ b]
+        feeds = [(rng.standard_normal((m, k)) / np.sqrt(k)).astype(np.float32),
+                 (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)]
+        work, unit, metric = 2.0 * m * n * k / 1e12, "TFLOP/s", f"fp32 GEMM TFLOP/s ({m}x{n}x{k}, 3xTF32)"
+    elif args.workload == "elementwise":
+        n = int(args.size or 8192)
+        a, b, c = g.input([n, n]), g.input([n, n]), g.input([1, n])
+        outs = [tt.relu(a * b + c) * 0.5 - tt.exp(-a)]
+        feeds = [rng.standard_normal(s).astype(np.float32) for s in ([n, n], [n, n], [1, n])]
+        work, unit, metric = (3 * n * n * 4 + n * 4) / 1e9, "GB/s", f"fused elementwise GB/s ({n}x{n})"
+    else:
+        r, c_ = (int(v) for v in (args.size or "8192,4096").split(","))
+        x = g.input([r, c_])
+        outs = [tt.sum(x, [1]), tt.mean(x, [1]), tt.max(x, [1]), tt.sum(tt.transpose(x, 0, 1), [0])]
+        feeds = [rng.uniform(-1, 1, (r, c_)).astype(np.float32)]
+        work, unit, metric = 4 * (r * c_ * 4 + r * 4) / 1e9, "GB/s", f"reductions GB/s ({r}x{c_}, 4 reductions)"
+    prog = tt.compile(g, outputs=outs)
+    ins = [tt.DeviceBuffer.from_numpy(f) for f in feeds]
+    res = [tt.DeviceBuffer(s) for s in prog.output_shapes]
+    ms = _time_program(torch, tt, prog, ins, res, args.steps, warm=args.warmup)
+    print(json.dumps({"metric": metric, "value": round(work / (ms * 1e-3), 2), "unit": unit, "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+                      "higher_is_better": True, "config": {"workload": args.workload, "size": args.size}}))
 
 
 if __name__ == "__main__":
