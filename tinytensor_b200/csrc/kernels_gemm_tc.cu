@@ -1,25 +1,34 @@
 // fp32-accurate GEMM on the 5th-generation tensor cores (sm_100a): 3xTF32.
 //
-// Each fp32 operand x is split once into hi = tf32_rna(x) (low 13 mantissa bits zero,
-// so the tensor core uses it exactly) and lo = x - hi (exact in fp32; the tensor core
-// keeps its top 11 significant bits).  C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi; the dropped
-// A_lo.B_lo term and the truncation of lo are O(2^-21) relative.
+// The tensor core reads a float32 operand as tf32 by dropping its low 13 mantissa
+// bits (verified bitwise on B200: feeding x or its truncation gives identical
+// products).  Each operand x is split into hi = trunc_tf32(x) and
+// lo = trunc_tf32(x - hi) (x - hi is exact in fp32); C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi,
+// and the dropped A_lo.B_lo term and the truncation of lo are O(2^-20) relative.
+// Both halves are stored with their low 13 bits already zero although the tensor core
+// would ignore them: on B200 the MMA main loop runs 6-10% faster on such operands
+// than on full-mantissa fp32 (same products; less switching under the power limit).
 //
 // Accumulation: the tensor core's fp32 accumulation does not round to nearest (its
 // error grows with the number of accumulation steps; measured ~7e-9 * K relative on
-// B200), so TMEM only accumulates CHUNKS of `chunk_kb` 32-wide K blocks (256 values of
-// K by default).  Two TMEM accumulators (2 x 256 columns) alternate: while the MMA
-// issuer fills one chunk, eight epilogue warps drain the previous one into fp32
-// registers with round-to-nearest adds.  With 256-wide chunks the product meets the
-// 1e-5 relative-Frobenius contract against the reference's fp32 matmul
-// (src/core/operators.cpp:235-319) at any K.
+// B200), so TMEM only accumulates CHUNKS of `chunk_kb` K blocks (256 values of K by
+// default).  Two TMEM accumulators (2 x 256 columns) alternate: while the MMA issuer
+// fills one chunk, eight epilogue warps drain the previous one into fp32 registers
+// with round-to-nearest adds.  The product then meets the 1e-5 relative-Frobenius
+// contract against the reference's fp32 matmul (src/core/operators.cpp:235-319) at
+// any K.
+//
+// Operand layout: hi and lo are written K-major (K contiguous, rows padded to 4
+// floats so TMA rows are 16-B aligned) whatever the view's strides; an M- or N-major
+// view is transposed through shared memory on the way.  (tcgen05 also reads
+// M/N-major tf32 tiles, in the 32-B-atom 128-B swizzle, but measured ~4% slower in
+// the main loop than K-major tiles, which outweighs the transposing copy.)
 //
 // Pipeline (one 128x256 output tile per CTA, 320 threads):
-//   split pre-pass : K-major hi/lo copies of both operands in scratch (M/N-major views
-//                    transposed through shared memory), K padded to 4 floats so rows
-//                    are 16-byte aligned for TMA;
-//   warp 0         : TMA producer, 2 stages x (A_hi, A_lo, B_hi, B_lo) 128-B swizzled
-//                    tiles of 32 floats along K, completion on mbarriers;
+//   split pre-pass : hi/lo of both operands in scratch (vectorised rows, or 32x32
+//                    shared-memory transposes for M/N-major views);
+//   warp 0         : TMA producer, STAGES x (A_hi, A_lo, B_hi, B_lo) swizzled tiles of
+//                    BK floats along K, completion on mbarriers;
 //   warp 1         : allocates 512 TMEM columns; one elected thread issues
 //                    tcgen05.mma.kind::tf32 (M=128, N=256, K=8; 3 products per step);
 //                    tcgen05.commit frees smem stages and publishes finished chunks;
@@ -46,15 +55,22 @@ namespace ttb {
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 32, STAGES = 2;
-constexpr int A_TILE = BM * BK * 4;                    // 16 KB
-constexpr int B_TILE = BN * BK * 4;                    // 32 KB
-constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;   // 96 KB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 2048;
+constexpr int BM = 128, BN = 256;
 constexpr uint32_t TMEM_COLS = 512;                    // two 256-column accumulators
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;           // 320
 constexpr long long WAIT_BUDGET = 4000000000LL;        // ~2 s of SM clock
+
+template <int BK>
+struct Cfg {
+    static constexpr int STAGES = 64 / BK;                       // 2 x 96 KB or 4 x 48 KB
+    static constexpr int A_TILE = BM * BK * 4;
+    static constexpr int B_TILE = BN * BK * 4;
+    static constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 2048;
+    static constexpr uint32_t KROW = BK * 4;                     // K-major row bytes: 128 or 64
+    static constexpr uint32_t KLAYOUT = BK == 32 ? 2u : 4u;      // descriptor SWIZZLE_128B / SWIZZLE_64B
+};
 
 enum : int { ST_TIMEOUT_EMPTY = 0x100, ST_TIMEOUT_FULL = 0x200, ST_TIMEOUT_TFULL = 0x300, ST_TIMEOUT_TEMPTY = 0x400 };
 
@@ -126,28 +142,35 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
-// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of 128 B,
-// 8-row swizzle atoms 1024 B apart (SBO); LBO is unused for swizzled K-major layouts.
-__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
+// Shared-memory matrix descriptor (sm_100 version 1).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
     uint64_t d = 0;
     d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-    d |= static_cast<uint64_t>(1u) << 16;             // LBO = 16 B
-    d |= static_cast<uint64_t>(1024u >> 4) << 32;     // SBO = 1024 B
-    d |= static_cast<uint64_t>(1u) << 46;             // descriptor version (sm_100)
-    d |= static_cast<uint64_t>(2u) << 61;             // SWIZZLE_128B
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(layout) << 61;
     return d;
+}
+
+// Descriptor of MMA k-step `ks` (8 tf32 of K) of a K-major operand tile: rows of BK
+// floats (BK*4 bytes), 8-row swizzle atoms (SBO); step = 32 B along the row.
+template <int BK>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t tile, int ks) {
+    return smem_desc(tile + static_cast<uint32_t>(ks) * 32u, 16u, 8u * Cfg<BK>::KROW, Cfg<BK>::KLAYOUT);
 }
 
 // Instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = 256.
 constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
                             (static_cast<uint32_t>(BM >> 4) << 24);
 
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -167,13 +190,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+template <int BK>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                    const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo, TcParams p) {
+    using C_ = Cfg<BK>;
+    constexpr int STAGES = C_::STAGES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* tiles = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C_::STAGE_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;   // [2] chunk accumulated  (MMA -> epilogue)
     uint64_t* tempty = tfull + 2;       // [2] chunk drained      (epilogue -> MMA)
@@ -221,13 +247,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int s = i % STAGES;
                 const uint32_t ph = (i / STAGES) & 1;
                 if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ST_TIMEOUT_EMPTY)) break;
-                uint8_t* st = tiles + s * STAGE_BYTES;
+                uint8_t* st = tiles + s * C_::STAGE_BYTES;
                 const int kx = (kb0 + i) * BK;
-                mbar_expect_tx(&full[s], STAGE_BYTES);
+                mbar_expect_tx(&full[s], C_::STAGE_BYTES);
                 tma_load_3d(st, &tm_ahi, &full[s], kx, m0, za);
-                tma_load_3d(st + A_TILE, &tm_alo, &full[s], kx, m0, za);
-                tma_load_3d(st + 2 * A_TILE, &tm_bhi, &full[s], kx, n0, zb);
-                tma_load_3d(st + 2 * A_TILE + B_TILE, &tm_blo, &full[s], kx, n0, zb);
+                tma_load_3d(st + C_::A_TILE, &tm_alo, &full[s], kx, m0, za);
+                tma_load_3d(st + 2 * C_::A_TILE, &tm_bhi, &full[s], kx, n0, zb);
+                tma_load_3d(st + 2 * C_::A_TILE + C_::B_TILE, &tm_blo, &full[s], kx, n0, zb);
                 issued = i + 1;
             }
             if (*abort_flag) {
@@ -252,16 +278,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (!mbar_wait(&full[s], ph, abort_flag, p.status, ST_TIMEOUT_FULL)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;");
                 const uint32_t acc = tmem + static_cast<uint32_t>(b * 256);
-                const uint32_t st = smem_u32(tiles + s * STAGE_BYTES);
-                const uint32_t ahi = st, alo = st + A_TILE, bhi = st + 2 * A_TILE, blo = st + 2 * A_TILE + B_TILE;
+                const uint32_t st = smem_u32(tiles + s * C_::STAGE_BYTES);
+                const uint32_t ahi = st, alo = st + C_::A_TILE, bhi = st + 2 * C_::A_TILE;
+                const uint32_t blo = st + 2 * C_::A_TILE + C_::B_TILE;
 #pragma unroll
                 for (int k = 0; k < BK / 8; ++k) {
-                    const uint32_t off = k * 32;  // 8 tf32 = 32 B along the swizzled 128-B row
-                    const uint64_t dah = desc_kmajor_sw128(ahi + off), dal = desc_kmajor_sw128(alo + off);
-                    const uint64_t dbh = desc_kmajor_sw128(bhi + off), dbl = desc_kmajor_sw128(blo + off);
-                    mma_tf32(acc, dah, dbh, (within | k) != 0);
-                    mma_tf32(acc, dah, dbl, 1u);
-                    mma_tf32(acc, dal, dbh, 1u);
+                    const uint64_t dah = operand_desc<BK>(ahi, k), dal = operand_desc<BK>(alo, k);
+                    const uint64_t dbh = operand_desc<BK>(bhi, k), dbl = operand_desc<BK>(blo, k);
+                    mma_tf32(acc, dah, dbh, kIdesc, (within | k) != 0);
+                    mma_tf32(acc, dah, dbl, kIdesc, 1u);
+                    mma_tf32(acc, dal, dbh, kIdesc, 1u);
                 }
                 mma_commit(&empty[s]);
                 if (within == p.chunk_kb - 1 || i == kcount - 1) mma_commit(&tfull[b]);
@@ -301,21 +327,23 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int col0 = n0 + h * 128 + j * 32;
-                    if (col0 >= p.N) break;
-                    float v[32];
+                    if (col0 < p.N) {
+                        float v[32];
 #pragma unroll
-                    for (int t = 0; t < 32; ++t) {
-                        v[t] = acc[j * 32 + t];
-                        if (p.epilogue == EP_RELU) v[t] = v[t] > 0.0f ? v[t] : 0.0f;
-                    }
-                    if (vec_ok && col0 + 32 <= p.N) {
+                        for (int t = 0; t < 32; ++t) {
+                            v[t] = acc[j * 32 + t];
+                            if (p.epilogue == EP_RELU) v[t] = v[t] > 0.0f ? v[t] : 0.0f;
+                        }
+                        if (vec_ok && col0 + 32 <= p.N) {
 #pragma unroll
-                        for (int t = 0; t < 32; t += 4)
-                            *reinterpret_cast<float4*>(crow + col0 + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
-                    } else {
+                            for (int t = 0; t < 32; t += 4)
+                                *reinterpret_cast<float4*>(crow + col0 + t) =
+                                    make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
+                        } else {
 #pragma unroll
-                        for (int t = 0; t < 32; ++t)
-                            if (col0 + t < p.N) crow[col0 + t] = v[t];
+                            for (int t = 0; t < 32; ++t)
+                                if (col0 + t < p.N) crow[col0 + t] = v[t];
+                        }
                     }
                 }
             }
@@ -342,88 +370,177 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     }
 }
 
-// ---- split pre-pass: X (rows R along M or N, K columns, any strides) -> hi/lo [b][R][Kp] ----
-__device__ __forceinline__ void split_one(float x, float& hi, float& lo) {
-    uint32_t h;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
-    hi = __uint_as_float(h);
-    lo = isfinite(x) ? __fsub_rn(x, hi) : 0.0f;
+// ---- split pre-pass ----
+// hi = trunc_tf32(x), lo = trunc_tf32(x - hi) (x - hi is exact in fp32).  NaN becomes
+// the canonical quiet NaN, whose payload survives the truncation; for +-inf lo = 0.
+__device__ __forceinline__ float trunc_tf32(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+    if (isfinite(x)) {
+        hi = trunc_tf32(x);
+        lo = trunc_tf32(__fsub_rn(x, hi));
+    } else {
+        hi = isnan(x) ? __uint_as_float(0x7FC00000u) : x;
+        lo = 0.0f;
+    }
 }
 
-// K contiguous (or general strides): one thread per element, k fastest.
-__global__ void __launch_bounds__(256) split_rowmajor_kernel(const float* __restrict__ X, float* __restrict__ hi,
-                                                             float* __restrict__ lo, int64_t R, int64_t K, int64_t Kp,
-                                                             int64_t s_r, int64_t s_k, int64_t s_b) {
-    const int64_t per = R * K;
+// View X[b][r][k] = X[b*s_b + r*s_r + k*s_k] -> hi/lo[b*l_b + r*l_r + k], one warp per
+// row r.  vec4 (s_k == 1, K % 4 == 0, X, s_r and s_b 16-B aligned) moves float4s.
+__global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ X, float* __restrict__ hi,
+                                                         float* __restrict__ lo, int64_t R, int64_t K, int64_t s_r,
+                                                         int64_t s_k, int64_t s_b, int64_t l_r, int64_t l_b,
+                                                         int vec4) {
     const int64_t b = blockIdx.y;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < per;
-         i += static_cast<int64_t>(gridDim.x) * 256) {
-        const int64_t r = i / K, k = i - r * K;
-        float h, l;
-        split_one(__ldg(X + b * s_b + r * s_r + k * s_k), h, l);
-        const int64_t o = (b * R + r) * Kp + k;
-        hi[o] = h;
-        lo[o] = l;
-    }
-}
-
-// R contiguous (an M- or N-major view): 32x32 tiles transposed through shared memory.
-__global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ X, float* __restrict__ hi,
-                                                              float* __restrict__ lo, int64_t R, int64_t K, int64_t Kp,
-                                                              int64_t s_k, int64_t s_b) {
-    __shared__ float th[32][33], tl[32][33];
-    const int64_t b = blockIdx.z;
-    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 32, k0 = static_cast<int64_t>(blockIdx.y) * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
-    for (int j = ty; j < 32; j += 8) {
-        const int64_t r = r0 + tx, k = k0 + j;
-        float h = 0.f, l = 0.f;
-        if (r < R && k < K) split_one(__ldg(X + b * s_b + k * s_k + r), h, l);
-        th[j][tx] = h;
-        tl[j][tx] = l;
-    }
-    __syncthreads();
-    for (int j = ty; j < 32; j += 8) {
-        const int64_t r = r0 + j, k = k0 + tx;
-        if (r < R && k < K) {
-            const int64_t o = (b * R + r) * Kp + k;
-            hi[o] = th[tx][j];
-            lo[o] = tl[tx][j];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* xb = X + b * s_b;
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp; r < R; r += static_cast<int64_t>(gridDim.x) * 8) {
+        const float* xr = xb + r * s_r;
+        float* hr = hi + b * l_b + r * l_r;
+        float* lr = lo + b * l_b + r * l_r;
+        if (vec4) {
+#pragma unroll 4
+            for (int64_t i = lane * 4; i < K; i += 128) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(xr + i));
+                float4 h, l;
+                split_tf32(x.x, h.x, l.x);
+                split_tf32(x.y, h.y, l.y);
+                split_tf32(x.z, h.z, l.z);
+                split_tf32(x.w, h.w, l.w);
+                *reinterpret_cast<float4*>(hr + i) = h;
+                *reinterpret_cast<float4*>(lr + i) = l;
+            }
+        } else {
+            for (int64_t i = lane; i < K; i += 32) split_tf32(__ldg(xr + i * s_k), hr[i], lr[i]);
         }
     }
 }
 
-int launch_split(const float* X, float* hi, float* lo, int64_t R, int64_t K, int64_t Kp, int64_t s_r, int64_t s_k,
-                 int64_t s_b, int64_t nb, cudaStream_t st) {
-    if (R == 0 || K == 0) return 0;
-    if (s_r == 1 && s_k != 1) {
-        dim3 grid(static_cast<unsigned>((R + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(nb));
-        split_transpose_kernel<<<grid, 256, 0, st>>>(X, hi, lo, R, K, Kp, s_k, s_b);
-    } else {
-        int64_t blocks = (R * K + 255) / 256;
-        if (blocks > 148 * 32) blocks = 148 * 32;
-        dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(nb));
-        split_rowmajor_kernel<<<grid, 256, 0, st>>>(X, hi, lo, R, K, Kp, s_r, s_k, s_b);
+// M/N-contiguous view (s_r == 1) -> K-major hi/lo[b*l_b + r*l_r + k]: tiles of 32 K x 128
+// rows go through shared memory.  Loads run along r (float4 when vec4: R % 4 == 0, X,
+// s_k and s_b 16-B aligned), stores along k.  Shared rows hold 32 float4 chunks, chunk c
+// of row k at position c ^ (k & 7), so the float4 writes (one row per warp) and the
+// float4 reads (one row per lane) are both free of bank conflicts.
+__global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ X, float* __restrict__ hi,
+                                                              float* __restrict__ lo, int64_t R, int64_t K,
+                                                              int64_t s_k, int64_t s_b, int64_t l_r, int64_t l_b,
+                                                              int vec4) {
+    __shared__ float4 th[32][32], tl[32][32];
+    const int64_t b = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float* xb = X + b * s_b;
+    float* hb = hi + b * l_b;
+    float* lb = lo + b * l_b;
+    const int64_t tk_n = (K + 31) / 32, tiles = tk_n * ((R + 127) / 128);
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int64_t tr = t / tk_n;
+        const int64_t r0 = tr * 128, k0 = (t - tr * tk_n) * 32;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int kk = warp + 8 * j;
+            const int64_t k = k0 + kk, r = r0 + 4 * lane;
+            float v[4];
+            if (vec4 && k < K && r < R) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(xb + k * s_k + r));
+                v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) v[q] = (k < K && r + q < R) ? __ldg(xb + k * s_k + r + q) : 0.0f;
+            }
+            float4 h, l;
+            split_tf32(v[0], h.x, l.x);
+            split_tf32(v[1], h.y, l.y);
+            split_tf32(v[2], h.z, l.z);
+            split_tf32(v[3], h.w, l.w);
+            th[kk][lane ^ (kk & 7)] = h;
+            tl[kk][lane ^ (kk & 7)] = l;
+        }
+        __syncthreads();
+        const int64_t k = k0 + lane;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c = warp + 8 * j;
+            const float4 h = th[lane][c ^ (lane & 7)], l = tl[lane][c ^ (lane & 7)];
+            const float hv[4] = {h.x, h.y, h.z, h.w}, lv[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int64_t r = r0 + 4 * c + q;
+                if (r < R && k < K) {
+                    hb[r * l_r + k] = hv[q];
+                    lb[r * l_r + k] = lv[q];
+                }
+            }
+        }
+        __syncthreads();
     }
-    return static_cast<int>(cudaGetLastError());
 }
 
 int64_t round4(int64_t x) { return (x + 3) / 4 * 4; }
 int64_t align256b(int64_t bytes) { return (bytes + 255) / 256 * 256; }
 
-void encode_kmajor(CUtensorMap* map, const float* base, int64_t K, int64_t Kp, int64_t rows, int64_t nb, int box_rows) {
-    cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(nb)};
-    cuuint64_t strides[2] = {static_cast<cuuint64_t>(Kp * 4), static_cast<cuuint64_t>(rows * Kp * 4)};
-    cuuint32_t box[3] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows), 1};
+// Compact K-major hi/lo arrays of one operand (rows R along M or N, K columns):
+// [nb][R][Kp], Kp = K rounded up to 4 floats so that every TMA row is 16-B aligned.
+struct OperandPlan {
+    int64_t nb = 1;          // batches stored (1 when broadcast over the batch)
+    int64_t lr = 0, lb = 0;  // row and batch strides (elements)
+};
+
+OperandPlan plan_operand(int64_t R, int64_t K, int64_t s_b, int64_t batch) {
+    OperandPlan o;
+    o.nb = s_b ? batch : 1;
+    o.lr = round4(K);
+    o.lb = R * o.lr;
+    return o;
+}
+
+int launch_split(const float* X, float* hi, float* lo, int64_t R, int64_t K, int64_t s_r, int64_t s_k, int64_t s_b,
+                 const OperandPlan& o, cudaStream_t st) {
+    if (R == 0 || K == 0) return 0;
+    const bool x16 = (reinterpret_cast<uintptr_t>(X) & 15) == 0 && (o.nb == 1 || s_b % 4 == 0);
+    if (s_r == 1 && s_k != 1 && R > 1 && K > 1) {
+        const bool vec4 = x16 && R % 4 == 0 && s_k % 4 == 0;
+        int64_t blocks = ((R + 127) / 128) * ((K + 31) / 32);
+        if (blocks > 148 * 8) blocks = 148 * 8;
+        split_transpose_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(o.nb)), 256, 0, st>>>(
+            X, hi, lo, R, K, s_k, s_b, o.lr, o.lb, vec4 ? 1 : 0);
+        return static_cast<int>(cudaGetLastError());
+    }
+    const bool vec4 = x16 && (s_k == 1 || K == 1) && K % 4 == 0 && s_r % 4 == 0;
+    int64_t blocks = (R + 7) / 8;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    split_rows_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(o.nb)), 256, 0, st>>>(
+        X, hi, lo, R, K, s_r, s_k, s_b, o.lr, o.lb, vec4 ? 1 : 0);
+    return static_cast<int>(cudaGetLastError());
+}
+
+// Tensor map of one compact operand array: dims {K, R, nb}, box {bk, box_rows, 1}.
+void encode_operand(CUtensorMap* map, const float* base, int64_t R, int64_t K, const OperandPlan& o, int bk,
+                    int box_rows) {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(R), static_cast<cuuint64_t>(o.nb)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(o.lr * 4), static_cast<cuuint64_t>(o.lb * 4)};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(bk), static_cast<cuuint32_t>(box_rows), 1};
     cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapSwizzle sw = bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     CUresult r = driver().tensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
-                                               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                                               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) fail(TT_ERR_RUNTIME, "cuTensorMapEncodeTiled: " + cu_error(r));
 }
 
 int64_t tiles_of(const GemmDesc& d) { return ((d.M + BM - 1) / BM) * ((d.N + BN - 1) / BN) * d.batch; }
+
+template <int BK>
+int launch_main(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
+                const TcParams& p, dim3 grid, cudaStream_t st) {
+    static std::once_flag once;
+    static cudaError_t err = cudaSuccess;
+    std::call_once(once, [] {
+        err = cudaFuncSetAttribute(gemm_tc_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Cfg<BK>::SMEM_BYTES);
+    });
+    if (err != cudaSuccess) return static_cast<int>(err);
+    gemm_tc_kernel<BK><<<grid, THREADS, Cfg<BK>::SMEM_BYTES, st>>>(ahi, alo, bhi, blo, p);
+    return static_cast<int>(cudaGetLastError());
+}
 
 }  // namespace
 
@@ -432,26 +549,35 @@ bool gemm_tc_supported(const GemmDesc& d) {
     return big && d.K >= 1 && d.batch <= 65535 && d.M < (1LL << 31) && d.N < (1LL << 31) && d.K < (1LL << 31);
 }
 
-// Split-K so that small tile grids still cover the GPU; each split keeps >= 16 K blocks.
+// Split-K so that small tile grids still cover the GPU; each split keeps >= 512 of K.
+#ifndef TT_GEMM_BK
+#define TT_GEMM_BK 32
+#endif
 void gemm_tc_plan(GemmDesc& d) {
-    const int64_t nkb = (d.K + BK - 1) / BK;
+    d.bk = TT_GEMM_BK;
+    const int64_t nkb = (d.K + d.bk - 1) / d.bk;
     const int64_t tiles = tiles_of(d);
     int64_t ks = 1;
     if (tiles < 120) {
         ks = (148 + tiles - 1) / tiles;
-        const int64_t cap = nkb / 16;
+        const int64_t cap = nkb / (512 / d.bk);
         if (ks > cap) ks = cap;
         if (ks < 1) ks = 1;
         if (ks * d.batch > 65535) ks = 65535 / d.batch;
     }
     const int64_t per = (nkb + ks - 1) / ks;
     d.ksplit = static_cast<int>((nkb + per - 1) / per);  // every split has >= 1 K block
+    d.chunk_kb = 256 / d.bk;                              // 256 values of K per TMEM chunk
+}
+
+// Compact hi (or lo) array size of one operand, elements.
+static int64_t operand_elems(int64_t R, int64_t K, int64_t s_b, int64_t batch) {
+    return (s_b ? batch : 1) * R * round4(K);
 }
 
 int64_t gemm_tc_scratch_bytes(const GemmDesc& d) {
-    const int64_t Kp = round4(d.K);
-    const int64_t ba = d.a_sb ? d.batch : 1, bb = d.b_sb ? d.batch : 1;
-    int64_t bytes = 2 * align256b(ba * d.M * Kp * 4) + 2 * align256b(bb * d.N * Kp * 4);
+    const int64_t a = operand_elems(d.M, d.K, d.a_sb, d.batch), b = operand_elems(d.N, d.K, d.b_sb, d.batch);
+    int64_t bytes = 2 * align256b(a * 4) + 2 * align256b(b * 4);
     if (d.ksplit > 1) bytes += align256b(d.batch * d.ksplit * d.M * d.N * 4);
     return bytes;
 }
@@ -459,34 +585,27 @@ int64_t gemm_tc_scratch_bytes(const GemmDesc& d) {
 int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
                    void* stream) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    static std::once_flag attr_once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(attr_once, [] {
-        attr_err = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    });
-    if (attr_err != cudaSuccess) return static_cast<int>(attr_err);
-    const int64_t Kp = round4(d.K);
-    const int64_t ba = d.a_sb ? d.batch : 1, bb = d.b_sb ? d.batch : 1;
+    const OperandPlan ap = plan_operand(d.M, d.K, d.a_sb, d.batch);
+    const OperandPlan bp = plan_operand(d.N, d.K, d.b_sb, d.batch);
+    const int64_t a_cap = align256b(operand_elems(d.M, d.K, d.a_sb, d.batch) * 4);
+    const int64_t b_cap = align256b(operand_elems(d.N, d.K, d.b_sb, d.batch) * 4);
     char* s = static_cast<char*>(scratch);
     float* ahi = reinterpret_cast<float*>(s);
-    s += align256b(ba * d.M * Kp * 4);
-    float* alo = reinterpret_cast<float*>(s);
-    s += align256b(ba * d.M * Kp * 4);
-    float* bhi = reinterpret_cast<float*>(s);
-    s += align256b(bb * d.N * Kp * 4);
-    float* blo = reinterpret_cast<float*>(s);
-    s += align256b(bb * d.N * Kp * 4);
-    float* partial = reinterpret_cast<float*>(s);
-    int rc = launch_split(A, ahi, alo, d.M, d.K, Kp, d.a_sm, d.a_sk, d.a_sb, ba, st);
+    float* alo = reinterpret_cast<float*>(s + a_cap);
+    float* bhi = reinterpret_cast<float*>(s + 2 * a_cap);
+    float* blo = reinterpret_cast<float*>(s + 2 * a_cap + b_cap);
+    float* partial = reinterpret_cast<float*>(s + 2 * a_cap + 2 * b_cap);
+    int rc = launch_split(A, ahi, alo, d.M, d.K, d.a_sm, d.a_sk, d.a_sb, ap, st);
     if (rc) return rc;
-    rc = launch_split(B, bhi, blo, d.N, d.K, Kp, d.b_sn, d.b_sk, d.b_sb, bb, st);
+    rc = launch_split(B, bhi, blo, d.N, d.K, d.b_sn, d.b_sk, d.b_sb, bp, st);
     if (rc) return rc;
+    const int bk = d.bk == 16 ? 16 : 32;
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-    encode_kmajor(&m_ahi, ahi, d.K, Kp, d.M, ba, BM);
-    encode_kmajor(&m_alo, alo, d.K, Kp, d.M, ba, BM);
-    encode_kmajor(&m_bhi, bhi, d.K, Kp, d.N, bb, BN);
-    encode_kmajor(&m_blo, blo, d.K, Kp, d.N, bb, BN);
-    const int64_t nkb = (d.K + BK - 1) / BK;
+    encode_operand(&m_ahi, ahi, d.M, d.K, ap, bk, BM);
+    encode_operand(&m_alo, alo, d.M, d.K, ap, bk, BM);
+    encode_operand(&m_bhi, bhi, d.N, d.K, bp, bk, BN);
+    encode_operand(&m_blo, blo, d.N, d.K, bp, bk, BN);
+    const int64_t nkb = (d.K + bk - 1) / bk;
     TcParams p;
     p.M = static_cast<int>(d.M);
     p.N = static_cast<int>(d.N);
@@ -495,7 +614,7 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
     p.b_batched = d.b_sb != 0;
     p.ksplit = d.ksplit;
     p.kb_per_split = static_cast<int>((nkb + d.ksplit - 1) / d.ksplit);
-    p.chunk_kb = d.chunk_kb > 0 ? d.chunk_kb : 8;
+    p.chunk_kb = d.chunk_kb > 0 ? d.chunk_kb : 256 / bk;
     p.status = status;
     if (d.ksplit > 1) {
         p.C = partial;
@@ -510,8 +629,8 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
     }
     dim3 grid(static_cast<unsigned>((d.N + BN - 1) / BN), static_cast<unsigned>((d.M + BM - 1) / BM),
               static_cast<unsigned>(d.batch * d.ksplit));
-    gemm_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(m_ahi, m_alo, m_bhi, m_blo, p);
-    rc = static_cast<int>(cudaGetLastError());
+    rc = bk == 16 ? launch_main<16>(m_ahi, m_alo, m_bhi, m_blo, p, grid, st)
+                  : launch_main<32>(m_ahi, m_alo, m_bhi, m_blo, p, grid, st);
     if (rc || d.ksplit == 1) return rc;
     const int64_t per = d.M * d.N;
     int64_t blocks = (per + 255) / 256;

@@ -52,7 +52,8 @@ struct GemmDesc {
     int epilogue = EP_NONE;
     int algo = 0;                          // chosen by plan_gemm
     int ksplit = 1;                        // tensor-core kernel: K split across CTAs
-    int chunk_kb = 8;                      // tensor-core kernel: 32-wide K blocks per TMEM chunk
+    int chunk_kb = 8;                      // tensor-core kernel: K blocks per TMEM chunk
+    int bk = 32;                           // tensor-core kernel: K per pipeline stage (16 or 32)
 };
 void plan_gemm(GemmDesc& d);  // picks the kernel variant for the shape/layout
 const char* gemm_algo_name(int algo);
