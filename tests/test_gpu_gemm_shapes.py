@@ -1,0 +1,110 @@
+"""GPU parity of the CUDA-core GEMM kernels for the shapes the tensor-core kernel does
+not take well: skinny products (N <= 16, or M <= 16 with the operand roles exchanged),
+products with K <= 16, and operands with odd strides.  Each case checks the kernel the
+planner chose (execution plan) and compares against the oracle's fp32 matmul and an
+fp64 product, at the GEMM tolerance (relative Frobenius)."""
+
+import numpy as np
+import pytest
+
+from parity import GEMM_FROB_RTOL, assert_norm
+
+import tinytensor_b200 as tt
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _data(rng, shape, k):
+    return (rng.standard_normal(shape) / np.sqrt(k)).astype(np.float32)
+
+
+def _check(c, a, b, rows=None):
+    """c = a @ b (2-D), on all rows or on sampled ones."""
+    if rows is None:
+        assert_norm(c, O.matmul(a, b), GEMM_FROB_RTOL)
+        assert_norm(c, a.astype(np.float64) @ b.astype(np.float64), GEMM_FROB_RTOL)
+    else:
+        idx = np.unique(np.random.default_rng(5).integers(0, a.shape[0], rows)).astype(np.int64)
+        assert_norm(c[idx], O.matmul_rows(a, b, idx), GEMM_FROB_RTOL)
+        assert_norm(c[idx], a[idx].astype(np.float64) @ b.astype(np.float64), GEMM_FROB_RTOL)
+
+
+@pytest.mark.parametrize("m,n,k", [(32768, 10, 4096), (3000, 16, 700), (129, 9, 1000), (200, 8, 5000), (77, 1, 300)])
+def test_skinny_n(m, n, k, cache_dir):
+    rng = np.random.default_rng(m + n + k)
+    a, b = _data(rng, (m, k), k), _data(rng, (k, n), k)
+    g = tt.Graph()
+    na, nb = g.input([m, k]), g.input([k, n])
+    prog = tt.compile(g, outputs=[na @ nb], cache_dir=cache_dir)
+    assert "simt_skinny[" in prog.execution_plan()
+    c = prog.run({na: a, nb: b}).numpy()
+    _check(c, a, b, rows=64 if m > 4096 else None)
+
+
+def test_skinny_n_transposed_a_long_k(cache_dir):
+    """The output layer's weight gradient: A = H^T (an M-major view), K = 32768, split-K."""
+    rng = np.random.default_rng(21)
+    m, n, k = 4096, 10, 32768
+    h = _data(rng, (k, m), k)
+    t = _data(rng, (k, n), k)
+    g = tt.Graph()
+    nh, nt = g.input([k, m]), g.input([k, n])
+    prog = tt.compile(g, outputs=[tt.transpose(nh, 0, 1) @ nt], cache_dir=cache_dir)
+    plan = prog.execution_plan()
+    assert "simt_skinny[" in plan and "splitk" in plan and "A:M" in plan
+    c = prog.run({nh: h, nt: t}).numpy()
+    _check(c, np.ascontiguousarray(h.T), t, rows=96)
+
+
+@pytest.mark.parametrize("m,n,k", [(10, 4096, 4096), (1, 300, 1000), (16, 515, 64)])
+def test_skinny_m(m, n, k, cache_dir):
+    rng = np.random.default_rng(m * 7 + n + k)
+    a, b = _data(rng, (m, k), k), _data(rng, (k, n), k)
+    g = tt.Graph()
+    na, nb = g.input([m, k]), g.input([k, n])
+    prog = tt.compile(g, outputs=[na @ nb], cache_dir=cache_dir)
+    assert "simt_skinny_t[" in prog.execution_plan()
+    _check(prog.run({na: a, nb: b}).numpy(), a, b)
+
+
+@pytest.mark.parametrize("m,n,k", [(32768, 4096, 10), (100, 130, 3), (64, 127, 16), (1000, 10, 1)])
+def test_small_k(m, n, k, cache_dir):
+    rng = np.random.default_rng(m + 3 * n + k)
+    a, b = _data(rng, (m, k), k), _data(rng, (k, n), k)
+    g = tt.Graph()
+    na, nb = g.input([m, k]), g.input([k, n])
+    prog = tt.compile(g, outputs=[na @ nb], cache_dir=cache_dir)
+    assert "simt_smallk[" in prog.execution_plan()
+    _check(prog.run({na: a, nb: b}).numpy(), a, b, rows=64 if m > 4096 else None)
+
+
+def test_small_k_transposed_b_relu_epilogue(cache_dir):
+    """relu(dY . W^T) with K = 10: B is a K-major view and ReLU is fused into the store."""
+    rng = np.random.default_rng(33)
+    m, n, k = 5000, 4096, 10
+    dy, w = _data(rng, (m, k), k), _data(rng, (n, k), k)
+    g = tt.Graph()
+    ndy, nw = g.input([m, k]), g.input([n, k])
+    prog = tt.compile(g, outputs=[tt.relu(ndy @ tt.transpose(nw, 0, 1))], cache_dir=cache_dir)
+    assert "simt_smallk[" in prog.execution_plan()
+    c = prog.run({ndy: dy, nw: w}).numpy()
+    idx = np.arange(0, m, 37, dtype=np.int64)
+    ref = np.maximum(dy[idx].astype(np.float64) @ w.T.astype(np.float64), 0.0)
+    assert_norm(c[idx], ref, GEMM_FROB_RTOL)
+
+
+def test_skinny_generic_strides_and_batch(cache_dir):
+    """Rows of 37 floats (not 16-B aligned: scalar loads) and a broadcast batch of 3."""
+    rng = np.random.default_rng(44)
+    bsz, m, n, k = 3, 1000, 10, 37
+    a = _data(rng, (bsz, m, k), k)
+    b = _data(rng, (k, n), k)
+    g = tt.Graph()
+    na, nb = g.input([bsz, m, k]), g.input([k, n])
+    prog = tt.compile(g, outputs=[na @ nb], cache_dir=cache_dir)
+    assert "simt_skinny[" in prog.execution_plan()
+    c = prog.run({na: a, nb: b}).numpy()
+    assert c.shape == (bsz, m, n)
+    for i in range(bsz):
+        _check(c[i], a[i], b)

@@ -128,54 +128,266 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const float* __restrict_
     }
 }
 
-// Narrow-N variant: one warp computes a 32-row x NB-column strip; used when N is small
-// (the 4096x10 output layer and its gradients).
-template <int NB, int EPI>
-__global__ void __launch_bounds__(256) gemm_narrow_kernel(const float* __restrict__ A, const float* __restrict__ B,
-                                                          float* __restrict__ C, int64_t M, int64_t N, int64_t K,
-                                                          int64_t a_sm, int64_t a_sk, int64_t a_sb, int64_t b_sk,
-                                                          int64_t b_sn, int64_t b_sb, int64_t c_sb) {
-    const int64_t bz = blockIdx.z;
-    A += bz * a_sb;
-    B += bz * b_sb;
-    C += bz * c_sb;
-    const int64_t m = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-    const int64_t n0 = static_cast<int64_t>(blockIdx.y) * NB;
-    __shared__ float Bs[64][NB];
-    float acc[NB];
+// Skinny products: at most 8*G output columns (N <= 16, or M <= 16 with the roles of A
+// and B exchanged).  Output (r, q) of batch b is sum_k X[b][r][k] * Y[b][k][q], with
+//   X[b][r][k] = X[b*x_sb + r*x_sr + k*x_sk],  Y[b][k][q] = Y[b*y_sb + k*y_sk + q*y_sq],
+// stored at C[z*c_sb + r*c_sr + q*c_sq], z = blockIdx.y (batch, or batch*ksplit + split
+// when K is split across CTAs and the partials are summed afterwards).
+// CTA: 128 rows x all columns over one K range, 128*G threads; thread (g, row) owns
+// columns 8g..8g+7 of one row.  X tiles (128 rows x 32 K) are staged transposed,
+// Xs[k][row], and double-buffered through registers; XMAJ names the contiguous index of
+// X (XM_K: k, XM_R: r, XM_GENERIC: neither) so that global loads are coalesced float4s.
+// Sums are kept in 256-K chunks added with RN adds: the rounding error stays that of a
+// 256-term sum at any K.  The kernel is bound by reading X once.
+enum { XM_GENERIC = 0, XM_K = 1, XM_R = 2 };
+
+template <int G, int XMAJ>
+__global__ void __launch_bounds__(128 * G) gemm_skinny_kernel(
+    const float* __restrict__ X, const float* __restrict__ Y, float* __restrict__ C, int64_t R, int64_t Q, int64_t K,
+    int64_t x_sr, int64_t x_sk, int64_t x_sb, int64_t y_sk, int64_t y_sq, int64_t y_sb, int64_t c_sr, int64_t c_sq,
+    int64_t c_sb, int64_t k_per_split, int ksplit, int epilogue) {
+    constexpr int TR = 128, TK = 32, NQ = 8 * G, THR = 128 * G;
+    constexpr int PAD = XMAJ == XM_R ? 4 : 1;  // XM_R stores float4 rows; others scalar, conflict-free at +1
+    constexpr int XV = TR * TK / 4 / THR;      // 4-float groups of the X tile per thread
+    constexpr int YV = TK * NQ / THR;          // Y tile elements per thread (2)
+    __shared__ __align__(16) float Xs[2][TK][TR + PAD];
+    __shared__ __align__(16) float Ys[2][TK][NQ];
+    const int tid = threadIdx.x;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * TR;
+    const int64_t bz = blockIdx.y / ksplit;
+    const int64_t kb = static_cast<int64_t>(blockIdx.y - bz * ksplit) * k_per_split;
+    const int64_t ke = K < kb + k_per_split ? K : kb + k_per_split;
+    X += bz * x_sb;
+    Y += bz * y_sb;
+    C += static_cast<int64_t>(blockIdx.y) * c_sb;
+
+    float xr[XV][4], yr[YV];
+    auto load = [&](int64_t k0) {
 #pragma unroll
-    for (int j = 0; j < NB; ++j) acc[j] = 0.0f;
-    for (int64_t k0 = 0; k0 < K; k0 += 64) {
-        __syncthreads();
-        for (int e = threadIdx.x; e < 64 * NB; e += 256) {
-            const int kk = e / NB, nn = e % NB;
-            const int64_t gk = k0 + kk, gn = n0 + nn;
-            Bs[kk][nn] = (gk < K && gn < N) ? __ldg(B + gk * b_sk + gn * b_sn) : 0.0f;
-        }
-        __syncthreads();
-        if (m < M) {
-            const int kmax = K - k0 < 64 ? static_cast<int>(K - k0) : 64;
-            for (int kk = 0; kk < kmax; ++kk) {
-                const float a = __ldg(A + m * a_sm + (k0 + kk) * a_sk);
+        for (int i = 0; i < XV; ++i) {
+            const int e = tid + i * THR;
+            if (XMAJ == XM_R) {
+                const int64_t k = k0 + e / 32, r = r0 + (e % 32) * 4;
+                if (k < ke && r + 3 < R) {
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(X + k * x_sk + r));
+                    xr[i][0] = v.x; xr[i][1] = v.y; xr[i][2] = v.z; xr[i][3] = v.w;
+                } else {
 #pragma unroll
-                for (int j = 0; j < NB; ++j) acc[j] = fmaf(a, Bs[kk][j], acc[j]);
+                    for (int j = 0; j < 4; ++j) xr[i][j] = (k < ke && r + j < R) ? __ldg(X + k * x_sk + r + j) : 0.0f;
+                }
+            } else {
+                const int64_t r = r0 + e / 8, k = k0 + (e % 8) * 4;
+                if (XMAJ == XM_K && r < R && k + 3 < ke) {
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(X + r * x_sr + k));
+                    xr[i][0] = v.x; xr[i][1] = v.y; xr[i][2] = v.z; xr[i][3] = v.w;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        xr[i][j] = (r < R && k + j < ke) ? __ldg(X + r * x_sr + (k + j) * x_sk) : 0.0f;
+                }
             }
         }
-    }
-    if (m < M) {
 #pragma unroll
-        for (int j = 0; j < NB; ++j) {
-            const int64_t gn = n0 + j;
-            if (gn < N) {
-                float v = acc[j];
-                if (EPI == EP_RELU) v = v > 0.0f ? v : 0.0f;
-                C[m * N + gn] = v;
+        for (int i = 0; i < YV; ++i) {
+            const int e = tid + i * THR;
+            const int64_t k = k0 + e / NQ, q = e % NQ;
+            yr[i] = (k < ke && q < Q) ? __ldg(Y + k * y_sk + q * y_sq) : 0.0f;
+        }
+    };
+    auto store = [&](int buf) {
+#pragma unroll
+        for (int i = 0; i < XV; ++i) {
+            const int e = tid + i * THR;
+            if (XMAJ == XM_R) {
+                *reinterpret_cast<float4*>(&Xs[buf][e / 32][(e % 32) * 4]) =
+                    make_float4(xr[i][0], xr[i][1], xr[i][2], xr[i][3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) Xs[buf][(e % 8) * 4 + j][e / 8] = xr[i][j];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < YV; ++i) {
+            const int e = tid + i * THR;
+            Ys[buf][e / NQ][e % NQ] = yr[i];
+        }
+    };
+
+    const int row = tid & (TR - 1), g = tid / TR;
+    float acc[8], tot[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = tot[j] = 0.0f;
+    load(kb);
+    store(0);
+    __syncthreads();
+    int buf = 0, tile = 0;
+    for (int64_t k0 = kb; k0 < ke; k0 += TK, ++tile) {
+        const bool more = k0 + TK < ke;
+        if (more) load(k0 + TK);
+#pragma unroll
+        for (int kk = 0; kk < TK; ++kk) {
+            const float a = Xs[buf][kk][row];
+            const float4 b0 = *reinterpret_cast<const float4*>(&Ys[buf][kk][g * 8]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Ys[buf][kk][g * 8 + 4]);
+            acc[0] = fmaf(a, b0.x, acc[0]);
+            acc[1] = fmaf(a, b0.y, acc[1]);
+            acc[2] = fmaf(a, b0.z, acc[2]);
+            acc[3] = fmaf(a, b0.w, acc[3]);
+            acc[4] = fmaf(a, b1.x, acc[4]);
+            acc[5] = fmaf(a, b1.y, acc[5]);
+            acc[6] = fmaf(a, b1.z, acc[6]);
+            acc[7] = fmaf(a, b1.w, acc[7]);
+        }
+        if ((tile & 7) == 7) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                tot[j] = __fadd_rn(tot[j], acc[j]);
+                acc[j] = 0.0f;
+            }
+        }
+        if (more) store(buf ^ 1);
+        __syncthreads();
+        buf ^= 1;
+    }
+    const int64_t r = r0 + row;
+    if (r < R) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int64_t q = g * 8 + j;
+            if (q < Q) {
+                float v = __fadd_rn(tot[j], acc[j]);
+                if (epilogue == EP_RELU) v = v > 0.0f ? v : 0.0f;
+                C[r * c_sr + q * c_sq] = v;
             }
         }
     }
 }
 
-enum Algo { ALGO_SIMT = 0, ALGO_NARROW = 1, ALGO_TC = 2 };
+// Products with K <= 16 (bound by writing C): a CTA computes a 64 x 128 tile from A
+// (64 x K) and B (K x 128) staged in shared memory; thread (ty, tx) owns rows ty + 8i
+// (i < 8) and columns 4tx..4tx+3, stored as float4 when C's rows allow it.
+template <int EPI>
+__global__ void __launch_bounds__(256) gemm_smallk_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                          float* __restrict__ C, int64_t M, int64_t N, int K,
+                                                          int64_t a_sm, int64_t a_sk, int64_t a_sb, int64_t b_sk,
+                                                          int64_t b_sn, int64_t b_sb, int64_t c_sb, int vec_store) {
+    __shared__ float As[64][17];
+    __shared__ __align__(16) float Bs[16][128];
+    const int tid = threadIdx.x, tx = tid & 31, ty = tid >> 5;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 64, n0 = static_cast<int64_t>(blockIdx.y) * 128;
+    const int64_t bz = blockIdx.z;
+    A += bz * a_sb;
+    B += bz * b_sb;
+    C += bz * c_sb;
+    for (int e = tid; e < 64 * 16; e += 256) {
+        const int rr = e >> 4, k = e & 15;
+        As[rr][k] = (m0 + rr < M && k < K) ? __ldg(A + (m0 + rr) * a_sm + k * a_sk) : 0.0f;
+    }
+    for (int e = tid; e < 16 * 128; e += 256) {
+        const int k = e >> 7, nn = e & 127;
+        Bs[k][nn] = (k < K && n0 + nn < N) ? __ldg(B + k * b_sk + (n0 + nn) * b_sn) : 0.0f;
+    }
+    __syncthreads();
+    const int64_t n = n0 + 4 * tx;
+#pragma unroll 2
+    for (int i = 0; i < 8; ++i) {
+        const int rr = ty + 8 * i;
+        const int64_t m = m0 + rr;
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int k = 0; k < K; ++k) {
+            const float a = As[rr][k];
+            const float4 b = *reinterpret_cast<const float4*>(&Bs[k][4 * tx]);
+            v[0] = fmaf(a, b.x, v[0]);
+            v[1] = fmaf(a, b.y, v[1]);
+            v[2] = fmaf(a, b.z, v[2]);
+            v[3] = fmaf(a, b.w, v[3]);
+        }
+        if (EPI == EP_RELU) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
+        }
+        if (m >= M) continue;
+        float* crow = C + m * N;
+        if (vec_store && n + 3 < N) {
+            *reinterpret_cast<float4*>(crow + n) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (n + j < N) crow[n + j] = v[j];
+        }
+    }
+}
+
+enum Algo { ALGO_SIMT = 0, ALGO_SKINNY = 1, ALGO_TC = 2, ALGO_SKINNY_T = 3, ALGO_SMALLK = 4 };
+
+// Operand roles of the skinny kernel: X has the long rows, Y the <= 16 columns.
+struct SkinnyView {
+    int64_t R, Q;
+    const float* X;
+    const float* Y;
+    int64_t x_sr, x_sk, x_sb, y_sk, y_sq, y_sb, c_sr, c_sq;
+};
+
+SkinnyView skinny_view(const GemmDesc& d, const float* A, const float* B) {
+    SkinnyView v;
+    if (d.algo == ALGO_SKINNY_T) {  // C^T = B^T . A^T: rows along N, columns along M
+        v = {d.N, d.M, B, A, d.b_sn, d.b_sk, d.b_sb, d.a_sk, d.a_sm, d.a_sb, 1, d.N};
+    } else {
+        v = {d.M, d.N, A, B, d.a_sm, d.a_sk, d.a_sb, d.b_sk, d.b_sn, d.b_sb, d.N, 1};
+    }
+    return v;
+}
+
+int64_t skinny_k_per_split(const GemmDesc& d) {
+    const int64_t per = (d.K + d.ksplit - 1) / d.ksplit;
+    return (per + 31) / 32 * 32;
+}
+
+template <int G, int XMAJ>
+void launch_skinny_t(const SkinnyView& v, const GemmDesc& d, float* out, int64_t out_sb, dim3 grid, cudaStream_t st) {
+    gemm_skinny_kernel<G, XMAJ><<<grid, 128 * G, 0, st>>>(v.X, v.Y, out, v.R, v.Q, d.K, v.x_sr, v.x_sk, v.x_sb, v.y_sk,
+                                                         v.y_sq, v.y_sb, v.c_sr, v.c_sq, out_sb, skinny_k_per_split(d),
+                                                         d.ksplit, d.ksplit > 1 ? EP_NONE : d.epilogue);
+}
+
+int launch_skinny(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, cudaStream_t st) {
+    const SkinnyView v = skinny_view(d, A, B);
+    const bool x16 = (reinterpret_cast<uintptr_t>(v.X) & 15) == 0 && (d.batch == 1 || v.x_sb % 4 == 0);
+    int xmaj = XM_GENERIC;
+    if (x16 && v.x_sk == 1 && v.x_sr % 4 == 0) xmaj = XM_K;
+    else if (x16 && v.x_sr == 1 && v.x_sk % 4 == 0) xmaj = XM_R;
+    float* out = d.ksplit > 1 ? static_cast<float*>(scratch) : C;
+    const int64_t out_sb = d.ksplit > 1 ? d.M * d.N : d.c_sb;
+    dim3 grid(static_cast<unsigned>((v.R + 127) / 128), static_cast<unsigned>(d.batch * d.ksplit));
+    const bool g2 = v.Q > 8;
+    if (g2) {
+        if (xmaj == XM_K) launch_skinny_t<2, XM_K>(v, d, out, out_sb, grid, st);
+        else if (xmaj == XM_R) launch_skinny_t<2, XM_R>(v, d, out, out_sb, grid, st);
+        else launch_skinny_t<2, XM_GENERIC>(v, d, out, out_sb, grid, st);
+    } else {
+        if (xmaj == XM_K) launch_skinny_t<1, XM_K>(v, d, out, out_sb, grid, st);
+        else if (xmaj == XM_R) launch_skinny_t<1, XM_R>(v, d, out, out_sb, grid, st);
+        else launch_skinny_t<1, XM_GENERIC>(v, d, out, out_sb, grid, st);
+    }
+    int rc = static_cast<int>(cudaGetLastError());
+    if (rc || d.ksplit == 1) return rc;
+    return launch_splitk_reduce(out, C, d.M * d.N, d.ksplit, d.batch, d.c_sb, d.epilogue, st);
+}
+
+// Split-K of the skinny kernel: enough CTAs for ~4 per SM, each split >= 256 of K.
+void plan_skinny(GemmDesc& d) {
+    const int64_t R = d.algo == ALGO_SKINNY_T ? d.N : d.M;
+    const int64_t ctas = (R + 127) / 128 * d.batch;
+    int64_t ks = 1;
+    if (ctas < 148 * 4) {
+        ks = (148 * 4 + ctas - 1) / ctas;
+        const int64_t cap = (d.K + 255) / 256;
+        if (ks > cap) ks = cap;
+        if (ks * d.batch > 65535) ks = 65535 / d.batch;
+        if (ks < 1) ks = 1;
+    }
+    d.ksplit = static_cast<int>(ks);
+}
 
 }  // namespace
 
@@ -187,28 +399,46 @@ void plan_gemm(GemmDesc& d) {
         d.b_sk = 1;
     }
     if (d.N == 1) d.b_sn = 1;
-    if (gemm_tc_supported(d)) {
+    d.ksplit = 1;
+    const bool batch_ok = d.batch <= 65535;
+    if (batch_ok && d.K <= 16 && (d.N + 127) / 128 <= 65535) {
+        d.algo = ALGO_SMALLK;
+    } else if (batch_ok && d.N <= 16) {
+        d.algo = ALGO_SKINNY;
+        plan_skinny(d);
+    } else if (batch_ok && d.M <= 16) {
+        d.algo = ALGO_SKINNY_T;
+        plan_skinny(d);
+    } else if (gemm_tc_supported(d)) {
         d.algo = ALGO_TC;
         gemm_tc_plan(d);
+    } else {
+        d.algo = ALGO_SIMT;
     }
-    else if (d.N <= 16) d.algo = ALGO_NARROW;
-    else d.algo = ALGO_SIMT;
 }
 
 const char* gemm_algo_name(int algo) {
     switch (algo) {
         case ALGO_TC: return "tcgen05_3xtf32";
-        case ALGO_NARROW: return "simt_narrow";
+        case ALGO_SKINNY: return "simt_skinny";
+        case ALGO_SKINNY_T: return "simt_skinny_t";
+        case ALGO_SMALLK: return "simt_smallk";
         default: return "simt";
     }
 }
 
-int64_t gemm_scratch_bytes(const GemmDesc& d) { return d.algo == ALGO_TC ? gemm_tc_scratch_bytes(d) : 0; }
+int64_t gemm_scratch_bytes(const GemmDesc& d) {
+    if (d.algo == ALGO_TC) return gemm_tc_scratch_bytes(d);
+    if ((d.algo == ALGO_SKINNY || d.algo == ALGO_SKINNY_T) && d.ksplit > 1) return d.batch * d.ksplit * d.M * d.N * 4;
+    return 0;
+}
 
 int gemm_launch_count(const GemmDesc& d) {
     if (d.M == 0 || d.N == 0 || d.batch == 0) return 0;
     if (d.K == 0) return static_cast<int>(d.batch);
-    return d.algo == ALGO_TC ? gemm_tc_launch_count(d) : 1;
+    if (d.algo == ALGO_TC) return gemm_tc_launch_count(d);
+    if (d.algo == ALGO_SKINNY || d.algo == ALGO_SKINNY_T) return d.ksplit > 1 ? 2 : 1;
+    return 1;
 }
 
 int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
@@ -226,15 +456,18 @@ int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, voi
         return 0;
     }
     if (d.algo == ALGO_TC) return launch_gemm_tc(d, A, B, C, scratch, status, stream);
-    if (d.algo == ALGO_NARROW) {
-        dim3 grid(static_cast<unsigned>((d.M + 255) / 256), static_cast<unsigned>((d.N + 15) / 16),
+    if (d.algo == ALGO_SKINNY || d.algo == ALGO_SKINNY_T) return launch_skinny(d, A, B, C, scratch, st);
+    if (d.algo == ALGO_SMALLK) {
+        dim3 grid(static_cast<unsigned>((d.M + 63) / 64), static_cast<unsigned>((d.N + 127) / 128),
                   static_cast<unsigned>(d.batch));
+        const int vec = d.N % 4 == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0 && d.c_sb % 4 == 0;
+        const int K = static_cast<int>(d.K);
         if (d.epilogue == EP_RELU)
-            gemm_narrow_kernel<16, EP_RELU><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, d.K, d.a_sm, d.a_sk, d.a_sb, d.b_sk,
-                                                                 d.b_sn, d.b_sb, d.c_sb);
+            gemm_smallk_kernel<EP_RELU><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, K, d.a_sm, d.a_sk, d.a_sb, d.b_sk,
+                                                              d.b_sn, d.b_sb, d.c_sb, vec);
         else
-            gemm_narrow_kernel<16, EP_NONE><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, d.K, d.a_sm, d.a_sk, d.a_sb, d.b_sk,
-                                                                 d.b_sn, d.b_sb, d.c_sb);
+            gemm_smallk_kernel<EP_NONE><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, K, d.a_sm, d.a_sk, d.a_sb, d.b_sk,
+                                                              d.b_sn, d.b_sb, d.c_sb, vec);
         return static_cast<int>(cudaGetLastError());
     }
     dim3 grid(static_cast<unsigned>((d.N + BN - 1) / BN), static_cast<unsigned>((d.M + BM - 1) / BM),

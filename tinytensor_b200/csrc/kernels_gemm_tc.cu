@@ -25,7 +25,7 @@
 // the main loop than K-major tiles, which outweighs the transposing copy.)
 //
 // Pipeline (one 128x256 output tile per CTA, 320 threads):
-//   split pre-pass : hi/lo of both operands in scratch (vectorised rows, or 32x32
+//   split pre-pass : hi/lo of both operands in scratch (vectorised rows, or 32 x 128
 //                    shared-memory transposes for M/N-major views);
 //   warp 0         : TMA producer, STAGES x (A_hi, A_lo, B_hi, B_lo) swizzled tiles of
 //                    BK floats along K, completion on mbarriers;
@@ -632,11 +632,15 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
     rc = bk == 16 ? launch_main<16>(m_ahi, m_alo, m_bhi, m_blo, p, grid, st)
                   : launch_main<32>(m_ahi, m_alo, m_bhi, m_blo, p, grid, st);
     if (rc || d.ksplit == 1) return rc;
-    const int64_t per = d.M * d.N;
+    return launch_splitk_reduce(partial, C, d.M * d.N, d.ksplit, d.batch, d.c_sb, d.epilogue, st);
+}
+
+int launch_splitk_reduce(const float* P, float* C, int64_t per, int ksplit, int64_t batch, int64_t c_sb, int epilogue,
+                         void* stream) {
     int64_t blocks = (per + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    splitk_reduce_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(d.batch)), 256, 0, st>>>(
-        partial, C, per, d.ksplit, d.c_sb, d.epilogue);
+    splitk_reduce_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(batch)), 256, 0,
+                           static_cast<cudaStream_t>(stream)>>>(P, C, per, ksplit, c_sb, epilogue);
     return static_cast<int>(cudaGetLastError());
 }
 

@@ -61,6 +61,10 @@ int64_t gemm_scratch_bytes(const GemmDesc& d);  // device scratch the chosen var
 int gemm_launch_count(const GemmDesc& d);        // kernels one launch_gemm issues
 int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
                 void* stream);
+// Sums split-K partials P[b][s][0..per) in split order into C[b*c_sb + i] and applies
+// the epilogue (deterministic).
+int launch_splitk_reduce(const float* P, float* C, int64_t per, int ksplit, int64_t batch, int64_t c_sb, int epilogue,
+                         void* stream);
 
 // ---- misc kernels (kernels_misc.cu) ----
 int launch_sgd(int n, float* const* params, const float* const* grads, float* const* vel, const int64_t* numels,
