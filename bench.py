@@ -165,20 +165,12 @@ def run_b200(args):
     tstream = torch.cuda.ExternalStream(stream.handle)
     dx, dt = tt.DeviceBuffer.from_numpy(xs), tt.DeviceBuffer.from_numpy(ts)
     dw = [tt.DeviceBuffer.from_numpy(a) for a in w]
-    # gradients written into one contiguous buffer so a single all-reduce covers them
-    sizes = [a.size for a in w]
-    gbuf = tt.DeviceBuffer([sum(sizes)])
-    offs = np.cumsum([0] + sizes)[:-1]
-    gptr = [gbuf.ptr + int(o) * 4 for o in offs]
-    dloss = tt.DeviceBuffer([])
     comm = tt.Communicator.from_torch_distributed(local) if world > 1 else None
-    opt = tt.SGD(dw, lr=LR)
+    trainer = tt.DataParallelSGD(prog, dw, lr=LR, comm=comm)
+    dloss = trainer.loss
 
     def step():
-        prog.run_device([dx, dt] + dw, [dloss] + gptr, stream)
-        if comm is not None:
-            comm.allreduce_sum(gbuf.ptr, int(sum(sizes)), stream)
-        opt.step(gptr, stream, lr_scale=1.0 / world)
+        trainer.step([dx, dt], stream)
 
     def barrier():
         torch.cuda.synchronize()

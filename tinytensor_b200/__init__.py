@@ -36,7 +36,7 @@ from .compiler import (  # noqa: F401
     launch_count,
     tensor,
 )
-from .dp import Communicator, shard_rows  # noqa: F401
+from .dp import Communicator, DataParallelSGD, broadcast_unique_id, shard_rows  # noqa: F401
 from .graph import (  # noqa: F401
     Graph,
     Node,

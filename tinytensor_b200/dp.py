@@ -3,29 +3,49 @@
 One process per GPU.  Rank r runs the full forward/backward program on rows
 [r*B/N, (r+1)*B/N) of the global batch; the weight gradients are summed across ranks
 with an NCCL all-reduce over NVLink (tt_dp_allreduce_sum) and the SGD step applies
-lr/N, so every replica stays bit-identical.  torch.distributed (any backend) is used
-only to hand the NCCL unique id from rank 0 to the others.
+lr/N, so every replica stays bit-identical.  Because the shards are equal, the mean of
+the shard losses is the global-batch mean and the summed shard gradients / N are its
+gradients.  torch.distributed (any backend) is used only to hand the NCCL unique id
+from rank 0 to the others.
 """
 
 import ctypes
 
+import numpy as np
+
 from . import _lib
 
-__all__ = ["Communicator", "shard_rows"]
+__all__ = ["Communicator", "DataParallelSGD", "shard_rows", "broadcast_unique_id"]
 
 
 def shard_rows(global_rows: int, rank: int, world: int):
     """Contiguous row range of `rank` (equal shards; global_rows % world == 0)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of size {world}")
     if global_rows % world:
         raise ValueError(f"global batch {global_rows} is not divisible by world size {world}")
     per = global_rows // world
     return rank * per, (rank + 1) * per
 
 
+def broadcast_unique_id() -> bytes:
+    """Rank 0 creates an NCCL unique id and the initialised torch.distributed group
+    (gloo or nccl) broadcasts it; every rank returns the same 128 bytes."""
+    import torch.distributed as dist
+
+    obj = [Communicator.new_unique_id() if dist.get_rank() == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    uid = obj[0]
+    if not isinstance(uid, bytes) or len(uid) != _lib.TT_DP_ID_BYTES:
+        raise _lib.RuntimeExecutionError("NCCL unique id broadcast returned a malformed id")
+    return uid
+
+
 class Communicator:
     def __init__(self, rank: int, world: int, device: int, unique_id: bytes):
         if len(unique_id) != _lib.TT_DP_ID_BYTES:
             raise ValueError("NCCL unique id must be 128 bytes")
+        self.handle = None
         h = ctypes.c_void_p()
         _lib.check(_lib.lib.tt_dp_init(rank, world, unique_id, device, ctypes.byref(h)))
         self.handle = h.value
@@ -42,10 +62,8 @@ class Communicator:
         """Bootstraps from an initialised torch.distributed group (rank 0 makes the id)."""
         import torch.distributed as dist
 
-        rank, world = dist.get_rank(), dist.get_world_size()
-        obj = [cls.new_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        return cls(rank, world, device, obj[0])
+        uid = broadcast_unique_id()
+        return cls(dist.get_rank(), dist.get_world_size(), device, uid)
 
     def allreduce_sum(self, buf, count: int | None = None, stream=None) -> None:
         ptr = getattr(buf, "ptr", buf)
@@ -63,3 +81,37 @@ class Communicator:
             self.close()
         except Exception:
             pass
+
+
+class DataParallelSGD:
+    """One data-parallel SGD step per call, all queued on one stream.
+
+    `program` is a compiled gradient program (tt.compile_gradients) whose inputs are
+    `batch_inputs + params` and whose outputs are `[loss] + [d loss / d p]`.  The
+    gradients land in one contiguous buffer so that a single all-reduce covers them;
+    then SGD applies lr / world to every parameter.  With comm=None (one process) the
+    step is the plain single-GPU step.
+    """
+
+    def __init__(self, program, params, lr: float = 0.01, momentum: float = 0.0, comm=None):
+        from .compiler import DeviceBuffer
+        from .optim import SGD
+
+        self.program = program
+        self.params = list(params)
+        self.comm = comm
+        self.world = comm.world if comm is not None else 1
+        self.sizes = [int(np.prod(p.shape, dtype=np.int64)) for p in self.params]
+        self.grads = DeviceBuffer([max(1, sum(self.sizes))])
+        offs = np.cumsum([0] + self.sizes)[:-1]
+        self.grad_ptrs = [self.grads.ptr + int(o) * 4 for o in offs]
+        self.loss = DeviceBuffer([])
+        self.opt = SGD(self.params, lr=lr, momentum=momentum)
+
+    def step(self, batch_inputs, stream) -> None:
+        """Queues forward+backward on the local shard, the gradient all-reduce and the
+        update; the local shard's loss is left in `self.loss` (device)."""
+        self.program.run_device(list(batch_inputs) + self.params, [self.loss] + self.grad_ptrs, stream)
+        if self.comm is not None:
+            self.comm.allreduce_sum(self.grads.ptr, sum(self.sizes), stream)
+        self.opt.step(self.grad_ptrs, stream, lr_scale=1.0 / self.world)
