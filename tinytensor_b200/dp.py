@@ -28,6 +28,15 @@ def shard_rows(global_rows: int, rank: int, world: int):
     return rank * per, (rank + 1) * per
 
 
+def _load_process_nccl() -> None:
+    """The library binds to the libnccl.so.2 already in the process; importing torch
+    first makes that torch's NCCL, so torch.distributed and this module share one."""
+    try:
+        import torch  # noqa: F401
+    except ImportError:
+        pass
+
+
 def broadcast_unique_id() -> bytes:
     """Rank 0 creates an NCCL unique id and the initialised torch.distributed group
     (gloo or nccl) broadcasts it; every rank returns the same 128 bytes."""
@@ -46,6 +55,7 @@ class Communicator:
         if len(unique_id) != _lib.TT_DP_ID_BYTES:
             raise ValueError("NCCL unique id must be 128 bytes")
         self.handle = None
+        _load_process_nccl()
         h = ctypes.c_void_p()
         _lib.check(_lib.lib.tt_dp_init(rank, world, unique_id, device, ctypes.byref(h)))
         self.handle = h.value
@@ -53,6 +63,7 @@ class Communicator:
 
     @staticmethod
     def new_unique_id() -> bytes:
+        _load_process_nccl()
         buf = ctypes.create_string_buffer(_lib.TT_DP_ID_BYTES)
         _lib.check(_lib.lib.tt_dp_unique_id(buf))
         return buf.raw
