@@ -34,7 +34,8 @@
 //                    tcgen05.commit frees smem stages and publishes finished chunks;
 //   warps 2..9     : drain chunks (tcgen05.ld 32 lanes x 32 columns), keep the row's
 //                    128 columns in registers, store to C (or to a split-K partial).
-// Split-K (ksplit > 1, for grids smaller than the GPU): CTA z handles a contiguous
+// Split-K (ksplit > 1, when the tile grid would leave the last wave of CTAs part-empty
+// or the GPU under-filled; chosen by gemm_tc_plan's wave model): CTA z handles a contiguous
 // range of K blocks and writes a partial tile; a reduce kernel sums the partials in
 // split order (deterministic) and applies the epilogue.
 // No TMA multicast: every CTA loads its own tiles (the kernel also runs inside
@@ -549,25 +550,45 @@ bool gemm_tc_supported(const GemmDesc& d) {
     return big && d.K >= 1 && d.batch <= 65535 && d.M < (1LL << 31) && d.N < (1LL << 31) && d.K < (1LL << 31);
 }
 
-// Split-K so that small tile grids still cover the GPU; each split keeps >= 512 of K.
+// Split-K choice by a wave model.  One 128x256 tile per CTA and one CTA per SM, so a
+// grid of n CTAs runs in ceil(n / 148) waves; a launch whose tile count leaves the
+// last wave part-empty (512 tiles = 3.46 waves) idles up to a quarter of the GPU.
+// For each candidate split count ks (splits of >= one 256-K TMEM chunk) the model
+// costs  waves(tiles * ks) * (K blocks per split + per-tile overhead)  plus the extra
+// HBM traffic of the partials (written, then read back by the reduce), converted to
+// K-block times, and keeps the cheapest.  Constants are B200 measurements: one
+// 32-wide K block of a tile takes ~1.27 us (3xTF32 at ~245 TFLOP/s over 148 SMs),
+// during which HBM moves ~8.3 MB.
 #ifndef TT_GEMM_BK
 #define TT_GEMM_BK 32
 #endif
 void gemm_tc_plan(GemmDesc& d) {
     d.bk = TT_GEMM_BK;
+    d.chunk_kb = 256 / d.bk;  // 256 values of K per TMEM chunk
     const int64_t nkb = (d.K + d.bk - 1) / d.bk;
     const int64_t tiles = tiles_of(d);
-    int64_t ks = 1;
-    if (tiles < 120) {
-        ks = (148 + tiles - 1) / tiles;
-        const int64_t cap = nkb / (512 / d.bk);
-        if (ks > cap) ks = cap;
-        if (ks < 1) ks = 1;
-        if (ks * d.batch > 65535) ks = 65535 / d.batch;
+    const double kb_us = 1.27 * d.bk / 32.0;
+    const double bytes_per_kb = 6.5e12 * kb_us * 1e-6;
+    const double tile_overhead_kb = 10.0;  // prologue, TMEM setup, epilogue drain and store (fitted)
+    const double out_bytes = static_cast<double>(d.M) * static_cast<double>(d.N) * 4.0 * static_cast<double>(d.batch);
+    int64_t best_ks = 1;
+    double best_cost = 0.0;
+    for (int64_t ks = 1; ks <= 16; ++ks) {
+        const int64_t per = (nkb + ks - 1) / ks;
+        const int64_t ks_eff = (nkb + per - 1) / per;
+        if (ks_eff != ks) continue;                        // same split as a smaller ks
+        if (ks > 1 && per < d.chunk_kb) break;             // splits shorter than a chunk
+        if (ks * d.batch > 65535) break;
+        if (ks > 1 && out_bytes * static_cast<double>(ks) > 2e9) break;  // partials' scratch
+        const int64_t waves = (tiles * ks + 147) / 148;
+        double cost = static_cast<double>(waves) * (static_cast<double>(per) + tile_overhead_kb);
+        if (ks > 1) cost += 2.0 * static_cast<double>(ks) * out_bytes / bytes_per_kb;
+        if (ks == 1 || cost < best_cost * 0.95) {         // a split must clearly pay for itself
+            best_cost = cost;
+            best_ks = ks;
+        }
     }
-    const int64_t per = (nkb + ks - 1) / ks;
-    d.ksplit = static_cast<int>((nkb + per - 1) / per);  // every split has >= 1 K block
-    d.chunk_kb = 256 / d.bk;                              // 256 values of K per TMEM chunk
+    d.ksplit = static_cast<int>(best_ks);
 }
 
 // Compact hi (or lo) array size of one operand, elements.
