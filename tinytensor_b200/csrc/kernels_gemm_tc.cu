@@ -358,6 +358,294 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// ---- CTA-pair variant (tcgen05 cta_group::2): 256 x 256 output tile per 2-CTA cluster ----
+// CTA rank r of the pair holds rows [128r, 128r+128) of the A tile and rows [128r, 128r+128)
+// of the 256-row B tile in its own shared memory, at the same offsets in both CTAs.  The
+// even CTA (the leader) issues tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 8): the
+// tensor cores of both SMs read A and B from both CTAs' shared memory and CTA r's TMEM
+// receives output rows [128r, 128r+128) x 256 columns.  Compared with one CTA per
+// 128x256 tile, each SM stores and reads half as many B bytes per K block, which is what
+// bounds the single-CTA main loop (shared-memory bandwidth).
+// Barriers: both CTAs' TMA loads complete on the LEADER's full[s] (the leader expects the
+// pair's bytes); the leader's commits arrive on empty[s] / tfull[b] in both CTAs (one
+// commit per CTA, the peer's barrier addressed through mapa); the epilogue warps of both
+// CTAs arrive on the leader's tempty[b] (16 arrivals).  Every wait is bounded as in the
+// single-CTA kernel, and both CTAs meet at a cluster barrier before TMEM is freed and
+// before either exits, so no arrival targets a CTA that has left.
+constexpr int PAIR_STAGES = 3;
+
+template <int BK>
+struct PairCfg {
+    static constexpr int TILE = 128 * BK * 4;               // 128 rows x BK floats (A or B half)
+    static constexpr int STAGE_BYTES = 4 * TILE;            // A_hi, A_lo, B_hi, B_lo of this CTA
+    static constexpr int SMEM_BYTES = PAIR_STAGES * STAGE_BYTES + 2048;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Address of this CTA's shared variable `p` in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+    return out;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on a barrier that receives arrivals from the peer CTA (cluster acquire).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  int* status, int code) {
+    const long long t0 = clock64();
+    uint32_t polls = 0;
+    while (!mbar_try_wait_cluster(bar, parity)) {
+        if (*abort_flag) return false;
+        if ((++polls & 255u) == 0 && *reinterpret_cast<volatile int*>(status) != 0) {
+            *abort_flag = 1;
+            return false;
+        }
+        if (clock64() - t0 > WAIT_BUDGET) {
+            *abort_flag = 1;
+            atomicCAS(status, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                                 int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4, %5}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrives on the barrier at cluster address `bar` when this thread's MMAs complete.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+                 : "memory");
+}
+
+// Instruction descriptor: D f32, A/B tf32, both K-major, M = 256 (the pair), N = 256.
+constexpr uint32_t kIdescPair = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(256 >> 3) << 17) |
+                                (static_cast<uint32_t>(256 >> 4) << 24);
+
+template <int BK>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+                        const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
+                        TcParams p) {
+    using C_ = PairCfg<BK>;
+    constexpr int STAGES = PAIR_STAGES;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* tiles = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C_::STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;   // [2] chunk accumulated  (leader's MMA -> both epilogues)
+    uint64_t* tempty = tfull + 2;       // [2] chunk drained      (both epilogues -> leader's MMA)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = (blockIdx.x >> 1) * 256;                 // pair's N range [n0, n0 + 256)
+    const int m0 = blockIdx.y * 256 + static_cast<int>(rank) * 128;  // this CTA's A rows / output rows
+    const int nb0 = n0 + static_cast<int>(rank) * 128;      // this CTA's half of B
+    const int zb_all = blockIdx.z;
+    const int batch = zb_all / p.ksplit, split = zb_all - batch * p.ksplit;
+    const int za = p.a_batched ? batch : 0, zb = p.b_batched ? batch : 0;
+    const int nkb_total = (p.K + BK - 1) / BK;
+    const int kb0 = split * p.kb_per_split;
+    const int kcount = max(0, min(nkb_total, kb0 + p.kb_per_split) - kb0);
+    const int nchunks = (kcount + p.chunk_kb - 1) / p.chunk_kb;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 2 * EPI_WARPS);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_ahi)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_bhi)) : "memory");
+            int issued = 0;
+            for (int i = 0; i < kcount; ++i) {
+                const int s = i % STAGES;
+                const uint32_t ph = (i / STAGES) & 1;
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ST_TIMEOUT_EMPTY)) break;
+                uint8_t* st = tiles + s * C_::STAGE_BYTES;
+                const int kx = (kb0 + i) * BK;
+                if (leader) mbar_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
+                const uint32_t fb = mapa_shared(&full[s], 0);
+                tma_load_3d_pair(st, &tm_ahi, fb, kx, m0, za);
+                tma_load_3d_pair(st + C_::TILE, &tm_alo, fb, kx, m0, za);
+                tma_load_3d_pair(st + 2 * C_::TILE, &tm_bhi, fb, kx, nb0, zb);
+                tma_load_3d_pair(st + 3 * C_::TILE, &tm_blo, fb, kx, nb0, zb);
+                issued = i + 1;
+            }
+            if (*abort_flag && issued > 0) {
+                if (leader) {
+                    // let the copies already issued land before shared memory goes away
+                    for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i) {
+                        const long long t0 = clock64();
+                        while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) && clock64() - t0 < WAIT_BUDGET) {
+                        }
+                    }
+                } else {
+                    // the follower's copies complete on the leader's barrier: give them time
+                    const long long t0 = clock64();
+                    while (clock64() - t0 < WAIT_BUDGET / 4) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (leader && lane == 0) {
+            for (int i = 0; i < kcount; ++i) {
+                const int s = i % STAGES;
+                const uint32_t ph = (i / STAGES) & 1;
+                const int c = i / p.chunk_kb, within = i - c * p.chunk_kb;
+                const int b = c & 1;
+                if (within == 0) {
+                    if (!mbar_wait_cluster(&tempty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.status, ST_TIMEOUT_TEMPTY))
+                        break;
+                }
+                if (!mbar_wait(&full[s], ph, abort_flag, p.status, ST_TIMEOUT_FULL)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t acc = tmem + static_cast<uint32_t>(b * 256);
+                const uint32_t st = smem_u32(tiles + s * C_::STAGE_BYTES);
+                const uint32_t ahi = st, alo = st + C_::TILE, bhi = st + 2 * C_::TILE, blo = st + 3 * C_::TILE;
+#pragma unroll
+                for (int k = 0; k < BK / 8; ++k) {
+                    const uint64_t dah = operand_desc<BK>(ahi, k), dal = operand_desc<BK>(alo, k);
+                    const uint64_t dbh = operand_desc<BK>(bhi, k), dbl = operand_desc<BK>(blo, k);
+                    mma_tf32_pair(acc, dah, dbh, kIdescPair, (within | k) != 0);
+                    mma_tf32_pair(acc, dah, dbl, kIdescPair, 1u);
+                    mma_tf32_pair(acc, dal, dbh, kIdescPair, 1u);
+                }
+                mma_commit_pair(mapa_shared(&empty[s], 0));
+                mma_commit_pair(mapa_shared(&empty[s], 1));
+                if (within == p.chunk_kb - 1 || i == kcount - 1) {
+                    mma_commit_pair(mapa_shared(&tfull[b], 0));
+                    mma_commit_pair(mapa_shared(&tfull[b], 1));
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // epilogue warp e (0..7): TMEM lanes 32*(warp%4).., columns 128*(e/4) .. +127
+        const int e = warp - 2, q = warp & 3, h = e >> 2;
+        const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+        float acc[128];
+#pragma unroll
+        for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+        bool ok = true;
+        for (int c = 0; c < nchunks; ++c) {
+            const int b = c & 1;
+            ok = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (c >> 1) & 1, abort_flag, p.status, ST_TIMEOUT_TFULL));
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t r[32];
+                tmem_ld32(tmem + lane_base + static_cast<uint32_t>(b * 256 + h * 128 + j * 32), r);
+#pragma unroll
+                for (int t = 0; t < 32; ++t) acc[j * 32 + t] = __fadd_rn(acc[j * 32 + t], __uint_as_float(r[t]));
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(&tempty[b], 0));
+        }
+        if (ok) {
+            const int row = m0 + q * 32 + lane;
+            float* crow = p.C + static_cast<int64_t>(zb_all) * p.c_bstride + static_cast<int64_t>(row) * p.ldc;
+            const bool vec_ok = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                                (p.c_bstride % 4 == 0);
+            if (row < p.M) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int col0 = n0 + h * 128 + j * 32;
+                    if (col0 < p.N) {
+                        float v[32];
+#pragma unroll
+                        for (int t = 0; t < 32; ++t) {
+                            v[t] = acc[j * 32 + t];
+                            if (p.epilogue == EP_RELU) v[t] = v[t] > 0.0f ? v[t] : 0.0f;
+                        }
+                        if (vec_ok && col0 + 32 <= p.N) {
+#pragma unroll
+                            for (int t = 0; t < 32; t += 4)
+                                *reinterpret_cast<float4*>(crow + col0 + t) =
+                                    make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
+                        } else {
+#pragma unroll
+                            for (int t = 0; t < 32; ++t)
+                                if (col0 + t < p.N) crow[col0 + t] = v[t];
+                        }
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    cluster_sync_all();  // all MMAs done, all remote arrivals delivered, in both CTAs
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
 // Sums split-K partials P[b][s][i] in split order and applies the epilogue.
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ P, float* __restrict__ C,
                                                             int64_t per, int ksplit, int64_t c_bstride, int epilogue) {
@@ -527,7 +815,11 @@ void encode_operand(CUtensorMap* map, const float* base, int64_t R, int64_t K, c
     if (r != CUDA_SUCCESS) fail(TT_ERR_RUNTIME, "cuTensorMapEncodeTiled: " + cu_error(r));
 }
 
-int64_t tiles_of(const GemmDesc& d) { return ((d.M + BM - 1) / BM) * ((d.N + BN - 1) / BN) * d.batch; }
+// CTAs of one launch without split-K: one per 128x256 tile, or two per 256x256 pair tile.
+int64_t ctas_of(const GemmDesc& d) {
+    if (d.pair) return 2 * ((d.M + 255) / 256) * ((d.N + 255) / 256) * d.batch;
+    return ((d.M + BM - 1) / BM) * ((d.N + BN - 1) / BN) * d.batch;
+}
 
 template <int BK>
 int launch_main(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
@@ -540,6 +832,20 @@ int launch_main(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
     });
     if (err != cudaSuccess) return static_cast<int>(err);
     gemm_tc_kernel<BK><<<grid, THREADS, Cfg<BK>::SMEM_BYTES, st>>>(ahi, alo, bhi, blo, p);
+    return static_cast<int>(cudaGetLastError());
+}
+
+template <int BK>
+int launch_pair(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
+                const TcParams& p, dim3 grid, cudaStream_t st) {
+    static std::once_flag once;
+    static cudaError_t err = cudaSuccess;
+    std::call_once(once, [] {
+        err = cudaFuncSetAttribute(gemm_tc_pair_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   PairCfg<BK>::SMEM_BYTES);
+    });
+    if (err != cudaSuccess) return static_cast<int>(err);
+    gemm_tc_pair_kernel<BK><<<grid, THREADS, PairCfg<BK>::SMEM_BYTES, st>>>(ahi, alo, bhi, blo, p);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -562,11 +868,15 @@ bool gemm_tc_supported(const GemmDesc& d) {
 #ifndef TT_GEMM_BK
 #define TT_GEMM_BK 32
 #endif
+#ifndef TT_GEMM_PAIR
+#define TT_GEMM_PAIR 1
+#endif
 void gemm_tc_plan(GemmDesc& d) {
     d.bk = TT_GEMM_BK;
     d.chunk_kb = 256 / d.bk;  // 256 values of K per TMEM chunk
+    d.pair = (TT_GEMM_PAIR && d.bk == 32 && d.M > 128) ? 1 : 0;
     const int64_t nkb = (d.K + d.bk - 1) / d.bk;
-    const int64_t tiles = tiles_of(d);
+    const int64_t tiles = ctas_of(d);
     const double kb_us = 1.27 * d.bk / 32.0;
     const double bytes_per_kb = 6.5e12 * kb_us * 1e-6;
     const double tile_overhead_kb = 10.0;  // prologue, TMEM setup, epilogue drain and store (fitted)
@@ -622,10 +932,11 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
     if (rc) return rc;
     const int bk = d.bk == 16 ? 16 : 32;
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+    const int b_rows = d.pair ? 128 : BN;  // a pair CTA holds half of the 256-row B tile
     encode_operand(&m_ahi, ahi, d.M, d.K, ap, bk, BM);
     encode_operand(&m_alo, alo, d.M, d.K, ap, bk, BM);
-    encode_operand(&m_bhi, bhi, d.N, d.K, bp, bk, BN);
-    encode_operand(&m_blo, blo, d.N, d.K, bp, bk, BN);
+    encode_operand(&m_bhi, bhi, d.N, d.K, bp, bk, b_rows);
+    encode_operand(&m_blo, blo, d.N, d.K, bp, bk, b_rows);
     const int64_t nkb = (d.K + bk - 1) / bk;
     TcParams p;
     p.M = static_cast<int>(d.M);
@@ -648,10 +959,16 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
         p.c_bstride = d.c_sb;
         p.epilogue = d.epilogue;
     }
-    dim3 grid(static_cast<unsigned>((d.N + BN - 1) / BN), static_cast<unsigned>((d.M + BM - 1) / BM),
-              static_cast<unsigned>(d.batch * d.ksplit));
-    rc = bk == 16 ? launch_main<16>(m_ahi, m_alo, m_bhi, m_blo, p, grid, st)
-                  : launch_main<32>(m_ahi, m_alo, m_bhi, m_blo, p, grid, st);
+    if (d.pair) {
+        dim3 grid(static_cast<unsigned>(2 * ((d.N + 255) / 256)), static_cast<unsigned>((d.M + 255) / 256),
+                  static_cast<unsigned>(d.batch * d.ksplit));
+        rc = launch_pair<32>(m_ahi, m_alo, m_bhi, m_blo, p, grid, st);
+    } else {
+        dim3 grid(static_cast<unsigned>((d.N + BN - 1) / BN), static_cast<unsigned>((d.M + BM - 1) / BM),
+                  static_cast<unsigned>(d.batch * d.ksplit));
+        rc = bk == 16 ? launch_main<16>(m_ahi, m_alo, m_bhi, m_blo, p, grid, st)
+                      : launch_main<32>(m_ahi, m_alo, m_bhi, m_blo, p, grid, st);
+    }
     if (rc || d.ksplit == 1) return rc;
     return launch_splitk_reduce(partial, C, d.M * d.N, d.ksplit, d.batch, d.c_sb, d.epilogue, st);
 }

@@ -54,6 +54,7 @@ struct GemmDesc {
     int ksplit = 1;                        // tensor-core kernel: K split across CTAs
     int chunk_kb = 8;                      // tensor-core kernel: K blocks per TMEM chunk
     int bk = 32;                           // tensor-core kernel: K per pipeline stage (16 or 32)
+    int pair = 0;                          // tensor-core kernel: 2-CTA (cta_group::2) 256x256 tiles
 };
 void plan_gemm(GemmDesc& d);  // picks the kernel variant for the shape/layout
 const char* gemm_algo_name(int algo);
