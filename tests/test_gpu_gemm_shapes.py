@@ -108,3 +108,41 @@ def test_skinny_generic_strides_and_batch(cache_dir):
     assert c.shape == (bsz, m, n)
     for i in range(bsz):
         _check(c[i], a[i], b)
+
+
+@pytest.mark.parametrize("sa,sb,kernel", [
+    ((6, 300, 512), (6, 512, 700), "tcgen05"),        # batched, M > 128: CTA-pair tiles, ragged M and N
+    ((3, 520, 1024), (1024, 384), "tcgen05"),         # B broadcast over the batch (stride 0)
+    ((4, 100, 2048), (4, 2048, 300), "tcgen05"),      # M <= 128: single-CTA tiles
+    ((2, 1, 64, 256), (5, 256, 96), "tcgen05"),       # broadcast batch dims [2,1] x [5] -> [2,5]
+])
+def test_batched_tensor_core(sa, sb, kernel, cache_dir):
+    rng = np.random.default_rng(sum(sa) + sum(sb))
+    k = sa[-1]
+    a, b = _data(rng, sa, k), _data(rng, sb, k)
+    g = tt.Graph()
+    na, nb = g.input(list(sa)), g.input(list(sb))
+    prog = tt.compile(g, outputs=[na @ nb], cache_dir=cache_dir)
+    assert kernel in prog.execution_plan()
+    c = prog.run({na: a, nb: b}).numpy()
+    ref64 = np.matmul(a.astype(np.float64), b.astype(np.float64))
+    assert c.shape == ref64.shape
+    assert_norm(c, O.matmul(a, b), GEMM_FROB_RTOL)
+    assert_norm(c, ref64, GEMM_FROB_RTOL)
+
+
+def test_batched_transposed_operands(cache_dir):
+    """Per-batch transposes of both operands (M- and K-major views inside a batch)."""
+    rng = np.random.default_rng(71)
+    bsz, m, n, k = 3, 384, 272, 640
+    at = _data(rng, (bsz, k, m), k)   # A = at^T per batch
+    bt = _data(rng, (bsz, n, k), k)   # B = bt^T per batch
+    g = tt.Graph()
+    nat, nbt = g.input([bsz, k, m]), g.input([bsz, n, k])
+    prog = tt.compile(g, outputs=[tt.transpose(nat, 1, 2) @ tt.transpose(nbt, 1, 2)], cache_dir=cache_dir)
+    assert "tcgen05" in prog.execution_plan()
+    c = prog.run({nat: at, nbt: bt}).numpy()
+    a = np.ascontiguousarray(np.transpose(at, (0, 2, 1)))
+    b = np.ascontiguousarray(np.transpose(bt, (0, 2, 1)))
+    assert_norm(c, O.matmul(a, b), GEMM_FROB_RTOL)
+    assert_norm(c, np.matmul(a.astype(np.float64), b.astype(np.float64)), GEMM_FROB_RTOL)

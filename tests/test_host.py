@@ -99,6 +99,21 @@ def test_transposes_fold_into_consumers(cache_dir):
     assert "reduce_sum/row" in plan  # the transposed column sum is a row reduction of x
 
 
+def test_batched_matmul_broadcasts(cache_dir):
+    """Whole-batch broadcast is a zero batch stride; a partial broadcast
+    ([2,1,..] x [5,..] -> [2,5,..]) is copied to the output's batch shape first."""
+    g = tt.Graph()
+    a, b = g.input([3, 64, 32]), g.input([32, 48])
+    plan = _host_compile(g, [a @ b], cache_dir).execution_plan()
+    assert "copy" not in plan and " b3 " in plan
+    g = tt.Graph()
+    a, b = g.input([2, 1, 64, 32]), g.input([5, 32, 48])
+    y = a @ b
+    assert y.shape == [2, 5, 64, 48]
+    plan = _host_compile(g, [y], cache_dir).execution_plan()
+    assert "copy[2, 5, 64, 32]" in plan and "copy[2, 5, 32, 48]" in plan and " b10 " in plan
+
+
 def test_fusion_respects_launch_dependencies(cache_dir):
     # sum(x) feeds back into an elementwise chain of x: the two regions must not merge
     g = tt.Graph()

@@ -333,6 +333,58 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         }
         return true;
     };
+    // The GEMM kernels take one batch stride per operand.  Aligned to the output's batch
+    // dims, the operand's batch offsets must be linear in the flattened batch index
+    // (offset = b * unit, unit 0 when the operand is broadcast over the whole batch);
+    // a partial broadcast such as [2,1,.,.] x [5,.,.] -> [2,5,.,.] is not.
+    auto batch_linear = [&](int q, const Shape& out) -> bool {
+        const Storage& s = p.st[static_cast<size_t>(q)];
+        const Shape& sh = g.nodes[static_cast<size_t>(q)].shape;
+        const size_t r = sh.size(), rc = out.size();
+        if (rc <= 2) return true;
+        const size_t nb = rc - 2, own = r - 2;
+        int64_t inner = 1, unit = 0;
+        bool have = false;
+        for (size_t d = nb; d-- > 0;) {
+            if (out[d] != 1) {
+                int64_t st = 0;
+                if (d + own >= nb) {
+                    const size_t od = d + own - nb;
+                    if (sh[od] != 1) st = s.strides[od];
+                }
+                if (st % inner != 0) return false;
+                if (have && st / inner != unit) return false;
+                unit = st / inner;
+                have = true;
+            }
+            inner *= out[d];
+        }
+        return true;
+    };
+    // Dense copy of `src` broadcast to the output's batch dims: [out batch..., rows, cols].
+    auto materialise_batch = [&](int src, const Shape& out) -> int {
+        const Shape& sh = g.nodes[static_cast<size_t>(src)].shape;
+        Shape full(out.begin(), out.end() - 2);
+        full.push_back(sh[sh.size() - 2]);
+        full.push_back(sh[sh.size() - 1]);
+        Node m;
+        m.op = TT_OP_EXPAND;
+        m.dtype = g.nodes[static_cast<size_t>(src)].dtype;
+        m.in = {src};
+        m.shape = full;
+        m.id = g.next_id;
+        int idx = g.add(m);
+        p.st.push_back(make_root(static_cast<size_t>(idx)));
+        p.region_of.push_back(-1);
+        Region r;
+        r.shape = full;
+        r.is_copy = true;
+        r.ext.push_back(src);
+        r.ext_access.push_back(broadcast_access(p.st[static_cast<size_t>(src)], src, sh, full));
+        r.stores.push_back(idx);
+        p.regions.push_back(r);
+        return idx;
+    };
     std::vector<int> launch_nodes;  // reduce / matmul nodes, original order
     g.nodes.reserve(N0 * 3 + 8);      // materialise() appends nodes: no reference is held across it
     for (size_t i = 0; i < N0; ++i) {
@@ -340,7 +392,10 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         if (op == TT_OP_MATMUL) {
             for (size_t k = 0; k < 2; ++k) {
                 const int src = g.nodes[i].in[k];
-                if (!gemm_ok(src, k == 0)) {
+                if (!batch_linear(src, g.nodes[i].shape)) {
+                    const Shape out = g.nodes[i].shape;
+                    g.nodes[i].in[k] = materialise_batch(src, out);
+                } else if (!gemm_ok(src, k == 0)) {
                     const int m = materialise(src);
                     g.nodes[i].in[k] = m;
                 }
