@@ -205,11 +205,10 @@ std::string generate_source(Plan& p) {
         std::string line;
         while (std::getline(ir, line)) ss << "//   " << line << "\n";
     }
-    ss << "\n// exp and tanh are evaluated in double and rounded once to float, which gives\n"
-          "// the correctly rounded float result except in vanishingly rare double-rounding\n"
-          "// cases (more accurate than a float libm such as the reference's std::exp).\n";
-    ss << "__device__ __forceinline__ float tt_exp(float x) { return (float)exp((double)x); }\n";
-    ss << "__device__ __forceinline__ float tt_tanh(float x) { return (float)tanh((double)x); }\n";
+    ss << "\n// exp and tanh: CUDA's float expf / tanhf (within 2 ulp, like the reference's float\n"
+          "// libm calls std::exp / std::tanh, which are not correctly rounded either).\n";
+    ss << "__device__ __forceinline__ float tt_exp(float x) { return expf(x); }\n";
+    ss << "__device__ __forceinline__ float tt_tanh(float x) { return tanhf(x); }\n";
     ss << "// Two-branch stable sigmoid in float, src/core/operators.cpp:211-232.\n";
     ss << "__device__ __forceinline__ float tt_sigmoid(float x) {\n"
           "  if (x >= 0.0f) return 1.0f / (1.0f + tt_exp(-x));\n"
