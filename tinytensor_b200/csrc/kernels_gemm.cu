@@ -263,59 +263,281 @@ __global__ void __launch_bounds__(128 * G) gemm_skinny_kernel(
     }
 }
 
-// Products with K <= 16 (bound by writing C): a CTA computes a 64 x 128 tile from A
-// (64 x K) and B (K x 128) staged in shared memory; thread (ty, tx) owns rows ty + 8i
-// (i < 8) and columns 4tx..4tx+3, stored as float4 when C's rows allow it.
-template <int EPI>
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, int bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Skinny products whose X is read in 16-B pieces (XM_K: k contiguous, XM_R: r
+// contiguous; 16-B aligned rows).  Same output mapping as gemm_skinny_kernel; here
+// X tiles (128 rows x 32 K, 16 KB) stream through a 4-stage cp.async ring straight
+// into shared memory (src-size zero-fill at the edges), and one thread owns one row and
+// all NQ (4..16, a multiple of 4) columns.  XM_K tiles stay row-major with each row's
+// 16-B chunks XOR-swizzled by the row (chunk c of row r at c ^ (r & 7)), so a warp's
+// per-row float4 reads are conflict-free; XM_R tiles are stored [k][row].  Sums are kept
+// in 256-K chunks added with RN adds, as in gemm_skinny_kernel.
+constexpr int SKA_TR = 128, SKA_TK = 32, SKA_ST = 4;
+
+template <int NQ>
+constexpr int skinny_async_smem() {
+    return SKA_ST * (SKA_TR * SKA_TK + SKA_TK * NQ) * 4;
+}
+
+template <int NQ, int XMAJ>
+__global__ void __launch_bounds__(128) gemm_skinny_async_kernel(
+    const float* __restrict__ X, const float* __restrict__ Y, float* __restrict__ C, int64_t R, int64_t Q, int64_t K,
+    int64_t x_sr, int64_t x_sk, int64_t x_sb, int64_t y_sk, int64_t y_sq, int64_t y_sb, int64_t c_sr, int64_t c_sq,
+    int64_t c_sb, int64_t k_per_split, int ksplit, int epilogue) {
+    constexpr int TR = SKA_TR, TK = SKA_TK, ST = SKA_ST;
+    extern __shared__ __align__(16) float ska_smem[];
+    float* Xs = ska_smem;                       // [ST][TR * TK]
+    float* Ys = ska_smem + ST * TR * TK;        // [ST][TK][NQ]
+    const int tid = threadIdx.x;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * TR;
+    const int64_t bz = blockIdx.y / ksplit;
+    const int64_t kb = static_cast<int64_t>(blockIdx.y - bz * ksplit) * k_per_split;
+    const int64_t ke = K < kb + k_per_split ? K : kb + k_per_split;
+    X += bz * x_sb;
+    Y += bz * y_sb;
+    C += static_cast<int64_t>(blockIdx.y) * c_sb;
+    const int ntiles = ke > kb ? static_cast<int>((ke - kb + TK - 1) / TK) : 0;
+
+    auto issue = [&](int t) {
+        const int s = t % ST;
+        const int64_t k0 = kb + static_cast<int64_t>(t) * TK;
+        float* xs = Xs + s * TR * TK;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int e = tid + i * 128;
+            int bytes = 0;
+            const float* src = X;
+            float* dst;
+            if (XMAJ == XM_K) {
+                const int rr = e >> 3, c = e & 7;
+                const int64_t r = r0 + rr, k = k0 + 4 * c;
+                if (r < R && k < ke) {
+                    bytes = ke - k >= 4 ? 16 : static_cast<int>(4 * (ke - k));
+                    src = X + r * x_sr + k;
+                }
+                dst = xs + rr * TK + ((c ^ (rr & 7)) << 2);
+            } else {
+                const int kk = e >> 5, c = e & 31;
+                const int64_t k = k0 + kk, r = r0 + 4 * c;
+                if (k < ke && r < R) {
+                    bytes = R - r >= 4 ? 16 : static_cast<int>(4 * (R - r));
+                    src = X + k * x_sk + r;
+                }
+                dst = xs + kk * TR + 4 * c;
+            }
+            cp_async16(dst, src, bytes);
+        }
+        float* ys = Ys + s * TK * NQ;
+        for (int e = tid; e < TK * NQ; e += 128) {
+            const int kk = e / NQ, q = e - kk * NQ;
+            const int64_t k = k0 + kk;
+            const bool in = k < ke && q < Q;
+            cp_async4(ys + e, in ? Y + k * y_sk + q * y_sq : Y, in ? 4 : 0);
+        }
+    };
+
+    float acc[NQ], tot[NQ];
+#pragma unroll
+    for (int j = 0; j < NQ; ++j) acc[j] = tot[j] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < ST - 1; ++t) {
+        if (t < ntiles) issue(t);
+        cp_async_commit();
+    }
+    const int rr = tid;
+    for (int t = 0; t < ntiles; ++t) {
+        cp_async_wait<ST - 2>();
+        __syncthreads();
+        if (t + ST - 1 < ntiles) issue(t + ST - 1);
+        cp_async_commit();
+        const int s = t % ST;
+        const float* xs = Xs + s * TR * TK;
+        const float* ys = Ys + s * TK * NQ;
+        if (XMAJ == XM_K) {
+#pragma unroll
+            for (int c = 0; c < TK / 4; ++c) {
+                const float4 a4 = *reinterpret_cast<const float4*>(xs + rr * TK + ((c ^ (rr & 7)) << 2));
+                const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float* yk = ys + (4 * c + j) * NQ;
+#pragma unroll
+                    for (int q4 = 0; q4 < NQ / 4; ++q4) {
+                        const float4 b = *reinterpret_cast<const float4*>(yk + 4 * q4);
+                        acc[4 * q4 + 0] = fmaf(av[j], b.x, acc[4 * q4 + 0]);
+                        acc[4 * q4 + 1] = fmaf(av[j], b.y, acc[4 * q4 + 1]);
+                        acc[4 * q4 + 2] = fmaf(av[j], b.z, acc[4 * q4 + 2]);
+                        acc[4 * q4 + 3] = fmaf(av[j], b.w, acc[4 * q4 + 3]);
+                    }
+                }
+            }
+        } else {
+#pragma unroll 8
+            for (int kk = 0; kk < TK; ++kk) {
+                const float a = xs[kk * TR + rr];
+                const float* yk = ys + kk * NQ;
+#pragma unroll
+                for (int q4 = 0; q4 < NQ / 4; ++q4) {
+                    const float4 b = *reinterpret_cast<const float4*>(yk + 4 * q4);
+                    acc[4 * q4 + 0] = fmaf(a, b.x, acc[4 * q4 + 0]);
+                    acc[4 * q4 + 1] = fmaf(a, b.y, acc[4 * q4 + 1]);
+                    acc[4 * q4 + 2] = fmaf(a, b.z, acc[4 * q4 + 2]);
+                    acc[4 * q4 + 3] = fmaf(a, b.w, acc[4 * q4 + 3]);
+                }
+            }
+        }
+        if ((t & 7) == 7) {
+#pragma unroll
+            for (int j = 0; j < NQ; ++j) {
+                tot[j] = __fadd_rn(tot[j], acc[j]);
+                acc[j] = 0.0f;
+            }
+        }
+    }
+    cp_async_wait<0>();
+    const int64_t r = r0 + rr;
+    if (r < R) {
+#pragma unroll
+        for (int j = 0; j < NQ; ++j) {
+            if (j < Q) {
+                float v = __fadd_rn(tot[j], acc[j]);
+                if (epilogue == EP_RELU) v = v > 0.0f ? v : 0.0f;
+                C[r * c_sr + j * c_sq] = v;
+            }
+        }
+    }
+}
+
+// Products with K <= 16 (bound by writing C).  A CTA owns one 128-column strip of C:
+// it stages B (K x 128) in shared memory once and keeps each thread's 4 columns of it
+// in registers (KP <= 16 float4s, K padded with zeros), then walks row blocks of 64
+// (blockIdx.y, grid-stride), double-buffering the A block (64 x K) through registers.
+// Thread (ty, tx) computes rows ty + 8i (i < 8) x columns 4tx..4tx+3 (float4 stores when
+// C's rows allow it).  Each output is one sequential fmaf sum over k < K (the zero
+// padding adds exact zeros).
+template <int KP, int EPI>
 __global__ void __launch_bounds__(256) gemm_smallk_kernel(const float* __restrict__ A, const float* __restrict__ B,
                                                           float* __restrict__ C, int64_t M, int64_t N, int K,
                                                           int64_t a_sm, int64_t a_sk, int64_t a_sb, int64_t b_sk,
                                                           int64_t b_sn, int64_t b_sb, int64_t c_sb, int vec_store) {
-    __shared__ float As[64][17];
+    __shared__ __align__(16) float As[2][64][16];
     __shared__ __align__(16) float Bs[16][128];
     const int tid = threadIdx.x, tx = tid & 31, ty = tid >> 5;
-    const int64_t m0 = static_cast<int64_t>(blockIdx.x) * 64, n0 = static_cast<int64_t>(blockIdx.y) * 128;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 128;
     const int64_t bz = blockIdx.z;
     A += bz * a_sb;
     B += bz * b_sb;
     C += bz * c_sb;
-    for (int e = tid; e < 64 * 16; e += 256) {
-        const int rr = e >> 4, k = e & 15;
-        As[rr][k] = (m0 + rr < M && k < K) ? __ldg(A + (m0 + rr) * a_sm + k * a_sk) : 0.0f;
-    }
-    for (int e = tid; e < 16 * 128; e += 256) {
+    for (int e = tid; e < KP * 128; e += 256) {
         const int k = e >> 7, nn = e & 127;
         Bs[k][nn] = (k < K && n0 + nn < N) ? __ldg(B + k * b_sk + (n0 + nn) * b_sn) : 0.0f;
     }
-    __syncthreads();
-    const int64_t n = n0 + 4 * tx;
-#pragma unroll 2
-    for (int i = 0; i < 8; ++i) {
-        const int rr = ty + 8 * i;
-        const int64_t m = m0 + rr;
-        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int k = 0; k < K; ++k) {
-            const float a = As[rr][k];
-            const float4 b = *reinterpret_cast<const float4*>(&Bs[k][4 * tx]);
-            v[0] = fmaf(a, b.x, v[0]);
-            v[1] = fmaf(a, b.y, v[1]);
-            v[2] = fmaf(a, b.z, v[2]);
-            v[3] = fmaf(a, b.w, v[3]);
-        }
-        if (EPI == EP_RELU) {
+    const int64_t row_tiles = (M + 63) / 64;
+    float ar[4];
+    auto load_a = [&](int64_t mt) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
+        for (int j = 0; j < 4; ++j) {
+            const int e = tid + 256 * j, rr = e >> 4, k = e & 15;
+            const int64_t m = mt * 64 + rr;
+            ar[j] = (m < M && k < K) ? __ldg(A + m * a_sm + k * a_sk) : 0.0f;
         }
-        if (m >= M) continue;
-        float* crow = C + m * N;
-        if (vec_store && n + 3 < N) {
-            *reinterpret_cast<float4*>(crow + n) = make_float4(v[0], v[1], v[2], v[3]);
-        } else {
+    };
+    auto store_a = [&](int buf) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                if (n + j < N) crow[n + j] = v[j];
+        for (int j = 0; j < 4; ++j) {
+            const int e = tid + 256 * j;
+            As[buf][e >> 4][e & 15] = ar[j];
         }
+    };
+    int64_t mt = blockIdx.y;
+    if (mt < row_tiles) {
+        load_a(mt);
+        store_a(0);
     }
+    __syncthreads();
+    float4 bk[KP];
+#pragma unroll
+    for (int k = 0; k < KP; ++k) bk[k] = *reinterpret_cast<const float4*>(&Bs[k][4 * tx]);
+    const int64_t n = n0 + 4 * tx;
+    int buf = 0;
+    for (; mt < row_tiles; mt += gridDim.y) {
+        const int64_t next = mt + gridDim.y;
+        if (next < row_tiles) load_a(next);
+#pragma unroll 2
+        for (int i = 0; i < 8; ++i) {
+            const int rr = ty + 8 * i;
+            const int64_t m = mt * 64 + rr;
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int k4 = 0; k4 < KP / 4; ++k4) {
+                const float4 a4 = *reinterpret_cast<const float4*>(&As[buf][rr][4 * k4]);
+                const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float4 b = bk[4 * k4 + j];
+                    v[0] = fmaf(av[j], b.x, v[0]);
+                    v[1] = fmaf(av[j], b.y, v[1]);
+                    v[2] = fmaf(av[j], b.z, v[2]);
+                    v[3] = fmaf(av[j], b.w, v[3]);
+                }
+            }
+            if (EPI == EP_RELU) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
+            }
+            if (m >= M) continue;
+            float* crow = C + m * N;
+            if (vec_store && n + 3 < N) {
+                *reinterpret_cast<float4*>(crow + n) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (n + j < N) crow[n + j] = v[j];
+            }
+        }
+        if (next < row_tiles) store_a(buf ^ 1);
+        __syncthreads();
+        buf ^= 1;
+    }
+}
+
+// One wave: a CTA per 128-column strip and row-block walker, as many as fit on the GPU.
+template <int KP>
+void launch_smallk_t(const GemmDesc& d, const float* A, const float* B, float* C, int vec, cudaStream_t st) {
+    static const int per_sm = [] {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemm_smallk_kernel<KP, EP_NONE>, 256, 0) != cudaSuccess)
+            n = 2;
+        return n > 0 ? n : 1;
+    }();
+    const int64_t col_tiles = (d.N + 127) / 128, row_tiles = (d.M + 63) / 64;
+    int64_t walkers = (148 * per_sm + col_tiles * d.batch - 1) / (col_tiles * d.batch);
+    if (walkers > row_tiles) walkers = row_tiles;
+    if (walkers > 65535) walkers = 65535;
+    if (walkers < 1) walkers = 1;
+    dim3 grid(static_cast<unsigned>(col_tiles), static_cast<unsigned>(walkers), static_cast<unsigned>(d.batch));
+    const int K = static_cast<int>(d.K);
+    if (d.epilogue == EP_RELU)
+        gemm_smallk_kernel<KP, EP_RELU><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, K, d.a_sm, d.a_sk, d.a_sb, d.b_sk,
+                                                              d.b_sn, d.b_sb, d.c_sb, vec);
+    else
+        gemm_smallk_kernel<KP, EP_NONE><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, K, d.a_sm, d.a_sk, d.a_sb, d.b_sk,
+                                                              d.b_sn, d.b_sb, d.c_sb, vec);
 }
 
 enum Algo { ALGO_SIMT = 0, ALGO_SKINNY = 1, ALGO_TC = 2, ALGO_SKINNY_T = 3, ALGO_SMALLK = 4 };
@@ -350,37 +572,55 @@ void launch_skinny_t(const SkinnyView& v, const GemmDesc& d, float* out, int64_t
                                                          d.ksplit, d.ksplit > 1 ? EP_NONE : d.epilogue);
 }
 
+template <int NQ, int XMAJ>
+void launch_skinny_async_t(const SkinnyView& v, const GemmDesc& d, float* out, int64_t out_sb, dim3 grid,
+                           cudaStream_t st) {
+    static bool attr = [] {
+        return cudaFuncSetAttribute(gemm_skinny_async_kernel<NQ, XMAJ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    skinny_async_smem<NQ>()) == cudaSuccess;
+    }();
+    (void)attr;
+    gemm_skinny_async_kernel<NQ, XMAJ><<<grid, 128, skinny_async_smem<NQ>(), st>>>(
+        v.X, v.Y, out, v.R, v.Q, d.K, v.x_sr, v.x_sk, v.x_sb, v.y_sk, v.y_sq, v.y_sb, v.c_sr, v.c_sq, out_sb,
+        skinny_k_per_split(d), d.ksplit, d.ksplit > 1 ? EP_NONE : d.epilogue);
+}
+
+template <int XMAJ>
+void launch_skinny_async(const SkinnyView& v, const GemmDesc& d, float* out, int64_t out_sb, dim3 grid,
+                         cudaStream_t st) {
+    if (v.Q <= 4) launch_skinny_async_t<4, XMAJ>(v, d, out, out_sb, grid, st);
+    else if (v.Q <= 8) launch_skinny_async_t<8, XMAJ>(v, d, out, out_sb, grid, st);
+    else if (v.Q <= 12) launch_skinny_async_t<12, XMAJ>(v, d, out, out_sb, grid, st);
+    else launch_skinny_async_t<16, XMAJ>(v, d, out, out_sb, grid, st);
+}
+
 int launch_skinny(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, cudaStream_t st) {
     const SkinnyView v = skinny_view(d, A, B);
     const bool x16 = (reinterpret_cast<uintptr_t>(v.X) & 15) == 0 && (d.batch == 1 || v.x_sb % 4 == 0);
-    int xmaj = XM_GENERIC;
-    if (x16 && v.x_sk == 1 && v.x_sr % 4 == 0) xmaj = XM_K;
-    else if (x16 && v.x_sr == 1 && v.x_sk % 4 == 0) xmaj = XM_R;
     float* out = d.ksplit > 1 ? static_cast<float*>(scratch) : C;
     const int64_t out_sb = d.ksplit > 1 ? d.M * d.N : d.c_sb;
     dim3 grid(static_cast<unsigned>((v.R + 127) / 128), static_cast<unsigned>(d.batch * d.ksplit));
-    const bool g2 = v.Q > 8;
-    if (g2) {
-        if (xmaj == XM_K) launch_skinny_t<2, XM_K>(v, d, out, out_sb, grid, st);
-        else if (xmaj == XM_R) launch_skinny_t<2, XM_R>(v, d, out, out_sb, grid, st);
-        else launch_skinny_t<2, XM_GENERIC>(v, d, out, out_sb, grid, st);
+    if (x16 && v.x_sk == 1 && v.x_sr % 4 == 0) {
+        launch_skinny_async<XM_K>(v, d, out, out_sb, grid, st);
+    } else if (x16 && v.x_sr == 1 && v.x_sk % 4 == 0) {
+        launch_skinny_async<XM_R>(v, d, out, out_sb, grid, st);
+    } else if (v.Q > 8) {
+        launch_skinny_t<2, XM_GENERIC>(v, d, out, out_sb, grid, st);
     } else {
-        if (xmaj == XM_K) launch_skinny_t<1, XM_K>(v, d, out, out_sb, grid, st);
-        else if (xmaj == XM_R) launch_skinny_t<1, XM_R>(v, d, out, out_sb, grid, st);
-        else launch_skinny_t<1, XM_GENERIC>(v, d, out, out_sb, grid, st);
+        launch_skinny_t<1, XM_GENERIC>(v, d, out, out_sb, grid, st);
     }
     int rc = static_cast<int>(cudaGetLastError());
     if (rc || d.ksplit == 1) return rc;
     return launch_splitk_reduce(out, C, d.M * d.N, d.ksplit, d.batch, d.c_sb, d.epilogue, st);
 }
 
-// Split-K of the skinny kernel: enough CTAs for ~4 per SM, each split >= 256 of K.
+// Split-K of the skinny kernels: enough CTAs for ~2 waves of 3 per SM, each split >= 256 of K.
 void plan_skinny(GemmDesc& d) {
     const int64_t R = d.algo == ALGO_SKINNY_T ? d.N : d.M;
     const int64_t ctas = (R + 127) / 128 * d.batch;
     int64_t ks = 1;
-    if (ctas < 148 * 4) {
-        ks = (148 * 4 + ctas - 1) / ctas;
+    if (ctas < 148 * 6) {
+        ks = (148 * 6 + ctas - 1) / ctas;
         const int64_t cap = (d.K + 255) / 256;
         if (ks > cap) ks = cap;
         if (ks * d.batch > 65535) ks = 65535 / d.batch;
@@ -458,16 +698,11 @@ int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, voi
     if (d.algo == ALGO_TC) return launch_gemm_tc(d, A, B, C, scratch, status, stream);
     if (d.algo == ALGO_SKINNY || d.algo == ALGO_SKINNY_T) return launch_skinny(d, A, B, C, scratch, st);
     if (d.algo == ALGO_SMALLK) {
-        dim3 grid(static_cast<unsigned>((d.M + 63) / 64), static_cast<unsigned>((d.N + 127) / 128),
-                  static_cast<unsigned>(d.batch));
         const int vec = d.N % 4 == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0 && d.c_sb % 4 == 0;
-        const int K = static_cast<int>(d.K);
-        if (d.epilogue == EP_RELU)
-            gemm_smallk_kernel<EP_RELU><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, K, d.a_sm, d.a_sk, d.a_sb, d.b_sk,
-                                                              d.b_sn, d.b_sb, d.c_sb, vec);
-        else
-            gemm_smallk_kernel<EP_NONE><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, K, d.a_sm, d.a_sk, d.a_sb, d.b_sk,
-                                                              d.b_sn, d.b_sb, d.c_sb, vec);
+        if (d.K <= 4) launch_smallk_t<4>(d, A, B, C, vec, st);
+        else if (d.K <= 8) launch_smallk_t<8>(d, A, B, C, vec, st);
+        else if (d.K <= 12) launch_smallk_t<12>(d, A, B, C, vec, st);
+        else launch_smallk_t<16>(d, A, B, C, vec, st);
         return static_cast<int>(cudaGetLastError());
     }
     dim3 grid(static_cast<unsigned>((d.N + BN - 1) / BN), static_cast<unsigned>((d.M + BM - 1) / BM),

@@ -720,30 +720,41 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __res
     float* hb = hi + b * l_b;
     float* lb = lo + b * l_b;
     const int64_t tk_n = (K + 31) / 32, tiles = tk_n * ((R + 127) / 128);
-    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    // the next tile's loads are issued before this tile's stores (software pipelining)
+    float v[4][4];
+    auto load = [&](int64_t t) {
+        const int64_t tr = t / tk_n;
+        const int64_t r0 = tr * 128, k0 = (t - tr * tk_n) * 32;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t k = k0 + warp + 8 * j, r = r0 + 4 * lane;
+            if (vec4 && k < K && r < R) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(xb + k * s_k + r));
+                v[j][0] = x.x; v[j][1] = x.y; v[j][2] = x.z; v[j][3] = x.w;
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) v[j][q] = (k < K && r + q < R) ? __ldg(xb + k * s_k + r + q) : 0.0f;
+            }
+        }
+    };
+    int64_t t = blockIdx.x;
+    if (t < tiles) load(t);
+    for (; t < tiles; t += gridDim.x) {
         const int64_t tr = t / tk_n;
         const int64_t r0 = tr * 128, k0 = (t - tr * tk_n) * 32;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int kk = warp + 8 * j;
-            const int64_t k = k0 + kk, r = r0 + 4 * lane;
-            float v[4];
-            if (vec4 && k < K && r < R) {
-                const float4 x = __ldg(reinterpret_cast<const float4*>(xb + k * s_k + r));
-                v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-            } else {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) v[q] = (k < K && r + q < R) ? __ldg(xb + k * s_k + r + q) : 0.0f;
-            }
             float4 h, l;
-            split_tf32(v[0], h.x, l.x);
-            split_tf32(v[1], h.y, l.y);
-            split_tf32(v[2], h.z, l.z);
-            split_tf32(v[3], h.w, l.w);
+            split_tf32(v[j][0], h.x, l.x);
+            split_tf32(v[j][1], h.y, l.y);
+            split_tf32(v[j][2], h.z, l.z);
+            split_tf32(v[j][3], h.w, l.w);
             th[kk][lane ^ (kk & 7)] = h;
             tl[kk][lane ^ (kk & 7)] = l;
         }
         __syncthreads();
+        if (t + gridDim.x < tiles) load(t + gridDim.x);
         const int64_t k = k0 + lane;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -787,8 +798,14 @@ int launch_split(const float* X, float* hi, float* lo, int64_t R, int64_t K, int
     const bool x16 = (reinterpret_cast<uintptr_t>(X) & 15) == 0 && (o.nb == 1 || s_b % 4 == 0);
     if (s_r == 1 && s_k != 1 && R > 1 && K > 1) {
         const bool vec4 = x16 && R % 4 == 0 && s_k % 4 == 0;
+        // one resident wave of grid-stride CTAs
+        static const int per_sm = [] {
+            int n = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, split_transpose_kernel, 256, 0) != cudaSuccess) n = 4;
+            return n > 0 ? n : 1;
+        }();
         int64_t blocks = ((R + 127) / 128) * ((K + 31) / 32);
-        if (blocks > 148 * 8) blocks = 148 * 8;
+        if (blocks > 148 * per_sm) blocks = 148 * per_sm;
         split_transpose_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(o.nb)), 256, 0, st>>>(
             X, hi, lo, R, K, s_k, s_b, o.lr, o.lb, vec4 ? 1 : 0);
         return static_cast<int>(cudaGetLastError());
