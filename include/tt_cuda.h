@@ -179,6 +179,16 @@ int tt_program_set_profiling(tt_program* p, int32_t enable);
 int tt_program_profile(const tt_program* p, int32_t cap, char* names, int32_t name_cap, float* ms,
                        int32_t* count);
 int tt_program_destroy(tt_program* p);
+/* Output-ready events (no counterpart in the reference, whose Executable::run is
+ * synchronous and single-stream).  events[k] (a tt_event_create handle, or NULL) is
+ * recorded on the run's stream as soon as output k is complete, so another stream can
+ * start work on it — e.g. the data-parallel all-reduce of one weight gradient — while
+ * the rest of the program still runs.  n <= number of outputs; n = 0 clears.  The
+ * program keeps the handles; the caller keeps them alive while it runs. */
+int tt_program_set_output_events(tt_program* p, void* const* events, int32_t n);
+/* Index of the launch after which output `output` is complete (-1: before the first),
+ * i.e. the order in which the output events fire. */
+int tt_program_output_step(tt_program* p, int32_t output, int32_t* step);
 
 /* ---- buffers (plain cudaMalloc / cudaMallocHost / cudaMemcpyAsync) ---- */
 enum tt_copy { TT_H2D = 1, TT_D2H = 2, TT_D2D = 3 };
@@ -190,6 +200,12 @@ int tt_memcpy(void* dst, const void* src, size_t bytes, int32_t kind, void* stre
 int tt_stream_create(void** stream);
 int tt_stream_destroy(void* stream);
 int tt_stream_sync(void* stream);
+/* Events for cross-stream ordering (cudaEventCreateWithFlags(DisableTiming) /
+ * cudaEventRecord / cudaStreamWaitEvent); no counterpart in the reference. */
+int tt_event_create(void** event);
+int tt_event_destroy(void* event);
+int tt_event_record(void* event, void* stream);
+int tt_stream_wait_event(void* stream, void* event);
 
 /* ---- optimiser: SGD.step (python/tinytensor/optim.py:18-35) on device ----
  * For each i: v = momentum*v + g (when momentum > 0, velocities[i] != NULL);

@@ -1,0 +1,50 @@
+"""Output-ready events on the GPU: a second stream that waits on a gradient's event
+and copies it sees the finished gradient while the program may still be running
+the launches after it (the data-parallel exchange relies on this)."""
+
+import numpy as np
+import pytest
+
+from parity import GEMM_FROB_RTOL, assert_norm
+
+import tinytensor_b200 as tt
+from tinytensor_b200 import _lib
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def test_output_events_order_gradient_copies(cache_dir):
+    rows, dims = 512, (256, 512, 512, 10)
+    rng = np.random.default_rng(8)
+    g = tt.Graph()
+    X, T = g.input([rows, dims[0]]), g.input([rows, dims[3]])
+    W = [g.input([a, b]) for a, b in zip(dims[:-1], dims[1:])]
+    d = tt.tanh(tt.relu(X @ W[0]) @ W[1]) @ W[2] - T
+    loss = tt.mean(d * d)
+    prog = tt.compile_gradients(g, loss, W, cache_dir=cache_dir)
+    x = rng.standard_normal((rows, dims[0])).astype(np.float32)
+    t = rng.standard_normal((rows, dims[3])).astype(np.float32)
+    ws = [(rng.standard_normal((a, b)) / np.sqrt(a)).astype(np.float32) for a, b in zip(dims[:-1], dims[1:])]
+    ins = [tt.DeviceBuffer.from_numpy(a) for a in [x, t] + ws]
+    outs = [tt.DeviceBuffer([])] + [tt.DeviceBuffer(w.shape) for w in ws]
+    copies = [tt.DeviceBuffer(w.shape) for w in ws]
+    events = [tt.Event() for _ in ws]
+    prog.set_output_events([None] + events)
+    steps = prog.output_steps()
+    assert steps[3] < steps[2] < steps[1]          # dW3, then dW2, then dW1
+    main, side = tt.Stream(), tt.Stream()
+    for _ in range(2):
+        prog.run_device(ins, outs, main)
+        for k in (2, 1, 0):                          # production order
+            events[k].wait(side)
+            _lib.check(_lib.lib.tt_memcpy(copies[k].ptr, outs[k + 1].ptr, copies[k].nbytes, _lib.D2D, side.handle))
+        side.synchronize()
+        main.synchronize()
+    assert prog.status() == 0
+    ref = O.gradients(g, loss, {X: x, T: t, W[0]: ws[0], W[1]: ws[1], W[2]: ws[2]}, W)
+    for k in range(3):
+        got = outs[k + 1].numpy()
+        assert np.array_equal(copies[k].numpy(), got)
+        assert_norm(got, ref[k], GEMM_FROB_RTOL)
+    prog.set_output_events([])

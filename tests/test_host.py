@@ -239,3 +239,25 @@ def test_unsupported_dtype_is_a_compile_error(cache_dir):
     a = g.input([4], dtype=tt.float64)
     with pytest.raises(tt.CompileError):
         _host_compile(g, [tt.relu(a)], cache_dir)
+
+
+def test_gradients_are_scheduled_early_with_output_steps(cache_dir):
+    """Launches that finish graph outputs run as soon as their inputs allow: in the MLP
+    gradient program dW2's GEMM precedes the dH1 GEMM, so its all-reduce can overlap it;
+    output_steps() gives the launch after which each output is complete."""
+    rows = 64
+    g = tt.Graph()
+    X, T = g.input([rows, 96]), g.input([rows, 10])
+    W1, W2, W3 = g.input([96, 256]), g.input([256, 256]), g.input([256, 10])
+    d = tt.tanh(tt.relu(X @ W1) @ W2) @ W3 - T
+    loss = tt.mean(d * d)
+    p = tt.compile_gradients(g, loss, [W1, W2, W3], cache_dir=cache_dir, flags=HOST)
+    launches = [line.strip() for line in p.execution_plan().splitlines() if line.strip().startswith("[")]
+    steps = p.output_steps()
+    assert len(steps) == 4 and len(set(steps)) == 4
+    for k, s in enumerate(steps):
+        assert 0 <= s < len(launches) and f"output:{k}" in launches[s]
+    loss_s, dw1_s, dw2_s, dw3_s = steps
+    assert dw3_s < dw2_s < dw1_s
+    dh1 = [i for i, l in enumerate(launches) if "[64x256x256" in l and "B:K" in l]
+    assert dh1 and dw2_s < dh1[0]

@@ -27,6 +27,7 @@ from ._lib import FLAG_HOST_ONLY, FLAG_NO_FUSION, FLAG_NO_GEMM_FUSION  # noqa: F
 from .compiler import (  # noqa: F401
     CompiledProgram,
     DeviceBuffer,
+    Event,
     PinnedBuffer,
     Stream,
     Tensor,

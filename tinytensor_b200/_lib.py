@@ -158,6 +158,8 @@ SIGNATURES = {
         [_VP, _I32, ctypes.c_char_p, _I32, ctypes.POINTER(_F), ctypes.POINTER(_I32)],
     ),
     "tt_program_destroy": (ctypes.c_int, [_VP]),
+    "tt_program_set_output_events": (ctypes.c_int, [_VP, ctypes.POINTER(_VP), _I32]),
+    "tt_program_output_step": (ctypes.c_int, [_VP, _I32, ctypes.POINTER(_I32)]),
     "tt_device_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(_VP)]),
     "tt_device_free": (ctypes.c_int, [_VP]),
     "tt_host_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(_VP)]),
@@ -166,6 +168,10 @@ SIGNATURES = {
     "tt_stream_create": (ctypes.c_int, [ctypes.POINTER(_VP)]),
     "tt_stream_destroy": (ctypes.c_int, [_VP]),
     "tt_stream_sync": (ctypes.c_int, [_VP]),
+    "tt_event_create": (ctypes.c_int, [ctypes.POINTER(_VP)]),
+    "tt_event_destroy": (ctypes.c_int, [_VP]),
+    "tt_event_record": (ctypes.c_int, [_VP, _VP]),
+    "tt_stream_wait_event": (ctypes.c_int, [_VP, _VP]),
     "tt_sgd_step": (
         ctypes.c_int,
         [_I32, ctypes.POINTER(_VP), ctypes.POINTER(_VP), ctypes.POINTER(_VP), ctypes.POINTER(_I64), _F, _F, _VP],

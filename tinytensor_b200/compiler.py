@@ -19,7 +19,7 @@ from ._lib import RuntimeExecutionError, ShapeError, TypeError
 from .graph import Graph, Node
 
 __all__ = ["compile", "compile_gradients", "CompiledProgram", "gradients", "Tensor", "tensor",
-           "DeviceBuffer", "Stream", "launch_count"]
+           "DeviceBuffer", "Stream", "Event", "launch_count"]
 
 
 def _default_cache_dir():
@@ -80,6 +80,27 @@ class Stream:
     def __del__(self):
         if getattr(self, "_own", False) and self.handle:
             _lib.lib.tt_stream_destroy(self.handle)
+            self.handle = None
+
+
+class Event:
+    """A CUDA event for ordering work across streams (no timing)."""
+
+    def __init__(self):
+        h = ctypes.c_void_p()
+        _lib.check(_lib.lib.tt_event_create(ctypes.byref(h)))
+        self.handle = h.value
+
+    def record(self, stream) -> None:
+        _lib.check(_lib.lib.tt_event_record(self.handle, getattr(stream, "handle", stream)))
+
+    def wait(self, stream) -> None:
+        """Makes `stream` wait (on the device) until this event has completed."""
+        _lib.check(_lib.lib.tt_stream_wait_event(getattr(stream, "handle", stream), self.handle))
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            _lib.lib.tt_event_destroy(self.handle)
             self.handle = None
 
 
@@ -238,6 +259,23 @@ class CompiledProgram:
         s = ctypes.c_int32()
         _lib.check(_lib.lib.tt_program_status(self._h, ctypes.byref(s)))
         return s.value
+
+    def set_output_events(self, events) -> None:
+        """events[k] (an Event or None) is recorded on the run's stream as soon as output k
+        is complete, while the rest of the program may still be running."""
+        self._out_events = list(events)
+        n = len(self._out_events)
+        arr = (ctypes.c_void_p * max(1, n))(*[e.handle if e is not None else None for e in self._out_events])
+        _lib.check(_lib.lib.tt_program_set_output_events(self._h, arr, n))
+
+    def output_steps(self):
+        """Per output, the launch after which it is complete (the order its event fires)."""
+        out = []
+        for k in range(self.num_outputs):
+            s = ctypes.c_int32()
+            _lib.check(_lib.lib.tt_program_output_step(self._h, k, ctypes.byref(s)))
+            out.append(s.value)
+        return out
 
     def set_profiling(self, enable: bool = True) -> None:
         _lib.check(_lib.lib.tt_program_set_profiling(self._h, int(enable)))

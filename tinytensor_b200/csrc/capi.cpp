@@ -100,6 +100,7 @@ struct tt_program {
     int64_t prof_runs = 0;
     bool prof_pending = false;
     bool has_tc = false;
+    std::vector<cudaEvent_t> out_events;  // caller's events, recorded when an output is complete
     std::mutex run_mutex;
 
     ~tt_program() {
@@ -315,6 +316,12 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
         }
         check_cuda(cudaEventRecord(p->events[0], stream), "cudaEventRecord");
     }
+    auto record_outputs = [&](int step) {
+        for (size_t k = 0; k < p->out_events.size(); ++k)
+            if (p->out_events[k] && pl.output_step[k] == step)
+                check_cuda(cudaEventRecord(p->out_events[k], stream), "cudaEventRecord(output)");
+    };
+    record_outputs(-1);
     for (size_t s = 0; s < pl.launches.size(); ++s) {
         const Launch& L = pl.launches[s];
         int rc = 0;
@@ -345,6 +352,7 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
         if (rc) fail(TT_ERR_RUNTIME, L.label + ": " + cudaGetErrorString(static_cast<cudaError_t>(rc)));
         g_launches += static_cast<uint64_t>(launches_of(pl, L));
         if (p->profiling) check_cuda(cudaEventRecord(p->events[s + 1], stream), "cudaEventRecord");
+        record_outputs(static_cast<int>(s));
     }
     p->prof_pending = p->profiling;
 }
@@ -422,6 +430,57 @@ int tt_program_run(tt_program* p, const void* const* inputs, void* const* output
                 fail(TT_ERR_DEVICE_STATUS, "a kernel gave up a bounded wait (status " + std::to_string(status) + ")");
             }
         }
+    });
+}
+
+int tt_program_set_output_events(tt_program* p, void* const* events, int32_t n) {
+    return guarded([&] {
+        if (!p) fail(TT_ERR_INVALID, "null program");
+        if (n < 0 || static_cast<size_t>(n) > p->out_shapes.size() || (n > 0 && !events))
+            fail(TT_ERR_INVALID, "events: expected at most " + std::to_string(p->out_shapes.size()) + " entries");
+        std::lock_guard<std::mutex> lk(p->run_mutex);
+        p->out_events.assign(static_cast<size_t>(n), nullptr);
+        for (int32_t k = 0; k < n; ++k) p->out_events[static_cast<size_t>(k)] = static_cast<cudaEvent_t>(events[k]);
+    });
+}
+
+int tt_program_output_step(tt_program* p, int32_t output, int32_t* step) {
+    return guarded([&] {
+        if (!p || !step) fail(TT_ERR_INVALID, "null argument");
+        if (output < 0 || static_cast<size_t>(output) >= p->plan.output_step.size())
+            fail(TT_ERR_INVALID, "output index out of range");
+        *step = p->plan.output_step[static_cast<size_t>(output)];
+    });
+}
+
+int tt_event_create(void** event) {
+    return guarded([&] {
+        if (!event) fail(TT_ERR_INVALID, "null argument");
+        cudaEvent_t e;
+        check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+        *event = e;
+    });
+}
+
+int tt_event_destroy(void* event) {
+    return guarded([&] {
+        if (event) check_cuda(cudaEventDestroy(static_cast<cudaEvent_t>(event)), "cudaEventDestroy");
+    });
+}
+
+int tt_event_record(void* event, void* stream) {
+    return guarded([&] {
+        if (!event) fail(TT_ERR_INVALID, "null event");
+        check_cuda(cudaEventRecord(static_cast<cudaEvent_t>(event), static_cast<cudaStream_t>(stream)),
+                   "cudaEventRecord");
+    });
+}
+
+int tt_stream_wait_event(void* stream, void* event) {
+    return guarded([&] {
+        if (!event) fail(TT_ERR_INVALID, "null event");
+        check_cuda(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), static_cast<cudaEvent_t>(event), 0),
+                   "cudaStreamWaitEvent");
     });
 }
 

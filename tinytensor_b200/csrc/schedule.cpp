@@ -491,6 +491,19 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
             indeg[u]++;
         }
     }
+    // Among ready launches, those that finish a graph output go first (then graph
+    // order): a caller waiting on an output (e.g. a gradient to all-reduce while the
+    // backward pass continues) can start as early as the dependencies allow.
+    for (Unit& u : units) {
+        bool writes_output = false;
+        for (int w : u.writes)
+            if (p.root_ref[static_cast<size_t>(w)].kind == BK_OUTPUT) writes_output = true;
+        if (u.type == LT_REGION && !p.regions[static_cast<size_t>(u.idx)].store_ref.empty()) {
+            for (const BufRef& b : p.regions[static_cast<size_t>(u.idx)].store_ref)
+                if (b.kind == BK_OUTPUT) writes_output = true;
+        }
+        if (writes_output && u.key < static_cast<int>(N)) u.key -= static_cast<int>(N) + 1;
+    }
     using QE = std::pair<int, int>;
     std::priority_queue<QE, std::vector<QE>, std::greater<QE>> ready;
     for (size_t u = 0; u < units.size(); ++u)
@@ -769,6 +782,19 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         }
     }
     (void)out_copy_region;
+    // launch after which each graph output is complete (its last writer)
+    p.output_step.assign(g.outputs.size(), -1);
+    for (size_t s = 0; s < p.launches.size(); ++s) {
+        const Launch& L = p.launches[s];
+        auto mark = [&](const BufRef& b) {
+            if (b.kind == BK_OUTPUT) p.output_step[static_cast<size_t>(b.index)] = static_cast<int>(s);
+        };
+        if (L.type == LT_REGION) {
+            for (const BufRef& b : p.regions[static_cast<size_t>(L.region)].store_ref) mark(b);
+        } else {
+            mark(L.out_ref);
+        }
+    }
     return p;
 }
 

@@ -36,6 +36,9 @@ struct Plan {
     int64_t total_alloc_bytes = 0, peak_planned_bytes = 0, theoretical_peak_bytes = 0;
     size_t reused_buffers = 0, num_intermediates = 0;
     size_t fused_regions = 0;
+    // per graph output: index of the launch after which it is complete (-1: written by
+    // no launch, complete when the program starts)
+    std::vector<int> output_step;
 };
 
 struct ScheduleOptions {

@@ -95,17 +95,22 @@ class Communicator:
 
 
 class DataParallelSGD:
-    """One data-parallel SGD step per call, all queued on one stream.
+    """One data-parallel SGD step per call.
 
     `program` is a compiled gradient program (tt.compile_gradients) whose inputs are
     `batch_inputs + params` and whose outputs are `[loss] + [d loss / d p]`.  The
-    gradients land in one contiguous buffer so that a single all-reduce covers them;
-    then SGD applies lr / world to every parameter.  With comm=None (one process) the
-    step is the plain single-GPU step.
+    gradients land in one contiguous buffer.  With a communicator, each gradient is
+    all-reduced on a second stream as soon as the program has produced it (the
+    program's output events; the scheduler runs output-producing launches as early as
+    their inputs allow), in the order the program produces them — the same on every
+    rank — so the exchange of one layer's gradient overlaps the backward pass of the
+    layers before it.  The update then waits for the exchange and applies lr / world.
+    With comm=None (one process) the step is the plain single-GPU step; overlap=False
+    all-reduces the whole buffer once after the program.
     """
 
-    def __init__(self, program, params, lr: float = 0.01, momentum: float = 0.0, comm=None):
-        from .compiler import DeviceBuffer
+    def __init__(self, program, params, lr: float = 0.01, momentum: float = 0.0, comm=None, overlap: bool = True):
+        from .compiler import DeviceBuffer, Event, Stream
         from .optim import SGD
 
         self.program = program
@@ -118,11 +123,26 @@ class DataParallelSGD:
         self.grad_ptrs = [self.grads.ptr + int(o) * 4 for o in offs]
         self.loss = DeviceBuffer([])
         self.opt = SGD(self.params, lr=lr, momentum=momentum)
+        self.overlap = bool(overlap and comm is not None and comm.world > 1)
+        if self.overlap:
+            self.comm_stream = Stream()
+            self.ready = [Event() for _ in self.params]
+            self.exchanged = Event()
+            program.set_output_events([None] + self.ready)
+            steps = program.output_steps()[1:1 + len(self.params)]
+            # exchange order = production order (ties: parameter order), identical on all ranks
+            self.order = sorted(range(len(self.params)), key=lambda i: (steps[i], i))
 
     def step(self, batch_inputs, stream) -> None:
         """Queues forward+backward on the local shard, the gradient all-reduce and the
         update; the local shard's loss is left in `self.loss` (device)."""
         self.program.run_device(list(batch_inputs) + self.params, [self.loss] + self.grad_ptrs, stream)
-        if self.comm is not None:
+        if self.overlap:
+            for i in self.order:
+                self.ready[i].wait(self.comm_stream)
+                self.comm.allreduce_sum(self.grad_ptrs[i], self.sizes[i], self.comm_stream)
+            self.exchanged.record(self.comm_stream)
+            self.exchanged.wait(stream)
+        elif self.comm is not None:
             self.comm.allreduce_sum(self.grads.ptr, sum(self.sizes), stream)
         self.opt.step(self.grad_ptrs, stream, lr_scale=1.0 / self.world)
