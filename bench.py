@@ -208,19 +208,23 @@ def run_b200(args):
     assert prog.status() == 0
 
     # end to end through the public API: per step H2D of this rank's (X, T) shard from
-    # pinned host memory, the step, D2H of the loss.
-    px, pt = tt.PinnedBuffer(xs.shape), tt.PinnedBuffer(ts.shape)
-    px.array[...] = xs
-    pt.array[...] = ts
+    # pinned host memory (DataParallelSGD.step_host: copies on a copy stream into
+    # alternating device slots, overlapping the previous step), the step, D2H of the loss.
+    # Two host batches alternate, as step_host asks.
+    hosts = []
+    for _ in range(2):
+        px, pt = tt.PinnedBuffer(xs.shape), tt.PinnedBuffer(ts.shape)
+        px.array[...] = xs
+        pt.array[...] = ts
+        hosts.append([px, pt])
     hloss = tt.PinnedBuffer([1])
     from tinytensor_b200 import _lib
+    trainer.step_host(hosts[1], stream)  # allocates the device slots outside the timed region
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(tstream)
-    for _ in range(args.steps):
-        _lib.check(_lib.lib.tt_memcpy(dx.ptr, px.ptr, dx.nbytes, _lib.H2D, stream.handle))
-        _lib.check(_lib.lib.tt_memcpy(dt.ptr, pt.ptr, dt.nbytes, _lib.H2D, stream.handle))
-        step()
+    for i in range(args.steps):
+        trainer.step_host(hosts[i % 2], stream)
         _lib.check(_lib.lib.tt_memcpy(hloss.ptr, dloss.ptr, 4, _lib.D2H, stream.handle))
     e1.record(tstream)
     barrier()

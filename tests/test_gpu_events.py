@@ -48,3 +48,42 @@ def test_output_events_order_gradient_copies(cache_dir):
         assert np.array_equal(copies[k].numpy(), got)
         assert_norm(got, ref[k], GEMM_FROB_RTOL)
     prog.set_output_events([])
+
+
+def test_step_host_matches_device_steps(cache_dir):
+    """DataParallelSGD.step_host (overlapped H2D into alternating slots) gives the same
+    weights, bit for bit, as step() on device-resident batches, batch by batch."""
+    rows, dims = 256, (128, 256, 256, 10)
+    rng = np.random.default_rng(13)
+    g = tt.Graph()
+    X, T = g.input([rows, dims[0]]), g.input([rows, dims[3]])
+    W = [g.input([a, b]) for a, b in zip(dims[:-1], dims[1:])]
+    d = tt.tanh(tt.relu(X @ W[0]) @ W[1]) @ W[2] - T
+    loss = tt.mean(d * d)
+    ws = [(rng.standard_normal((a, b)) / np.sqrt(a)).astype(np.float32) for a, b in zip(dims[:-1], dims[1:])]
+    batches = [(rng.standard_normal((rows, dims[0])).astype(np.float32),
+                rng.standard_normal((rows, dims[3])).astype(np.float32)) for _ in range(4)]
+    results = []
+    for host in (False, True):
+        prog = tt.compile_gradients(g, loss, W, cache_dir=cache_dir)
+        params = [tt.DeviceBuffer.from_numpy(w) for w in ws]
+        trainer = tt.DataParallelSGD(prog, params, lr=0.05)
+        stream = tt.Stream()
+        hosts = [[tt.PinnedBuffer([rows, dims[0]]), tt.PinnedBuffer([rows, dims[3]])] for _ in range(2)]
+        for i, (x, t) in enumerate(batches):
+            if host:
+                hosts[i % 2][0].array[...] = x
+                hosts[i % 2][1].array[...] = t
+                trainer.step_host(hosts[i % 2], stream)
+                if i % 2 == 1:
+                    stream.synchronize()   # both host buffers are reused by the next two steps
+            else:
+                dev = [tt.DeviceBuffer.from_numpy(x), tt.DeviceBuffer.from_numpy(t)]
+                trainer.step(dev, stream)
+                stream.synchronize()
+                del dev
+        stream.synchronize()
+        assert prog.status() == 0
+        results.append([p.numpy() for p in params])
+    for a, b in zip(*results):
+        assert np.array_equal(a, b)

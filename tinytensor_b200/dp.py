@@ -133,6 +133,38 @@ class DataParallelSGD:
             # exchange order = production order (ties: parameter order), identical on all ranks
             self.order = sorted(range(len(self.params)), key=lambda i: (steps[i], i))
 
+    def step_host(self, host_inputs, stream) -> None:
+        """step() with the batch in page-locked host memory (PinnedBuffer per input).
+        This call's host-to-device copies run on a copy stream into one of two device
+        slots, so they overlap the previous step still running on the GPU; the step
+        waits for its own copies, and a slot is refilled only after the step that read
+        it has finished.  The copies read the host buffers asynchronously: keep a
+        buffer unchanged until the next step_host call (or a synchronize) — e.g.
+        alternate two host buffers."""
+        from .compiler import DeviceBuffer, Event, Stream
+
+        if getattr(self, "_slots", None) is None:
+            self._slots = [[DeviceBuffer(h.shape) for h in host_inputs] for _ in range(2)]
+            self._copy_stream = Stream()
+            self._copied = [Event(), Event()]
+            self._consumed = [Event(), Event()]
+            self._consumed_pending = [False, False]
+            self._slot = 0
+        j = self._slot
+        bufs = self._slots[j]
+        if self._consumed_pending[j]:
+            self._consumed[j].wait(self._copy_stream)
+        for h, b in zip(host_inputs, bufs):
+            if h.array.nbytes != b.nbytes:
+                raise ValueError("host batch shapes changed between steps")
+            _lib.check(_lib.lib.tt_memcpy(b.ptr, h.ptr, b.nbytes, _lib.H2D, self._copy_stream.handle))
+        self._copied[j].record(self._copy_stream)
+        self._copied[j].wait(stream)
+        self.step(bufs, stream)
+        self._consumed[j].record(stream)
+        self._consumed_pending[j] = True
+        self._slot ^= 1
+
     def step(self, batch_inputs, stream) -> None:
         """Queues forward+backward on the local shard, the gradient all-reduce and the
         update; the local shard's loss is left in `self.loss` (device)."""
