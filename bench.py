@@ -240,19 +240,27 @@ def run_b200(args):
         dims = top_lbl.split("[")[1].split()[0].split("x")
         m, n, k = (int(v) for v in dims)
         gemm_flops = 2.0 * m * n * k
-    tf32_peak = peaks["bf16_tflops"] / 2.0
-    eff_peak = tf32_peak / 3.0  # 3xTF32: three TF32 products per fp32-accurate product
+    # The dominant launch is timed inside a long step, so its denominator is the
+    # sustained (power-capped) bf16 figure; the burst-based fraction is reported beside it.
+    sustained = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    eff_peak = sustained / 2.0 / 3.0        # TF32 = bf16/2; 3xTF32: three TF32 products per fp32 product
+    burst_peak = peaks["bf16_tflops"] / 2.0 / 3.0
+    achieved = gemm_flops / (top_ms * 1e-3) / 1e12 if gemm_flops else None
     roofline = {
         "kernel": top_lbl,
         "bound": "tensor",
-        "achieved": round(gemm_flops / (top_ms * 1e-3) / 1e12, 2) if gemm_flops else None,
+        "achieved": round(achieved, 2) if achieved else None,
         "peak": round(eff_peak, 1),
         "unit": "TFLOP/s",
-        "frac": round(gemm_flops / (top_ms * 1e-3) / 1e12 / eff_peak, 4) if gemm_flops else None,
+        "frac": round(achieved / eff_peak, 4) if achieved else None,
         "traffic": load_traffic(top_lbl),
-        "peak_source": f"{peak_src}: bf16_tflops/2 (TF32) /3 (3xTF32 products), fp32-equivalent",
+        "peak_source": f"{peak_src} sustained bf16 (bf16_tflops_sustained) /2 (TF32) /3 (3xTF32 products), "
+                       "fp32-equivalent",
+        "frac_of_burst_peak": round(achieved / burst_peak, 4) if achieved else None,
+        "burst_peak": round(burst_peak, 1),
         "avg_ms": round(top_ms, 4),
-        "timed": "CUDA events on the launch stream around the GEMM launch (its hi/lo split pre-pass included)",
+        "timed": "CUDA events on the launch stream around the GEMM launch (its hi/lo split pre-pass and "
+                 "split-K reduce included)",
     }
     total_prof = sum(t for _, t in prof)
     step_profile = [{"launch": lbl, "ms": round(t, 4), "share": round(t / total_prof, 4)}
