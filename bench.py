@@ -338,6 +338,41 @@ def components(tt, torch, args, peaks, peak_src):
         ew[f"{n}x{n}"] = {"ms": round(ms, 5), "GB/s": round(nbytes / ms / 1e6, 1),
                           "frac_of_measured_hbm": round(nbytes / ms / 1e6 / hbm, 3),
                           "note": "fits in L2 (126 MB): repeated calls hit L2" if n == 1024 else "> L2"}
+        if n == 1024:
+            # launch-bound at this size: 100 calls captured in one CUDA graph, replayed
+            st = tt.Stream()
+            ts = torch.cuda.ExternalStream(st.handle)
+            graph = tt.CudaGraph()
+            with graph.capture(st):
+                for _ in range(100):
+                    prog.run_device(ins, out, st)
+            graph.replay(st)
+            st.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(ts)
+            for _ in range(5):
+                graph.replay(st)
+            e1.record(ts)
+            st.synchronize()
+            gms = e0.elapsed_time(e1) / 500
+            ew["1024x1024_cuda_graph"] = {"ms": round(gms, 5), "GB/s": round(nbytes / gms / 1e6, 1),
+                                          "note": "100 calls per graph, L2-resident"}
+            # one call after writing 512 MB elsewhere (L2 flushed): HBM-cold latency
+            flush = torch.empty(128 * 1024 * 1024, dtype=torch.float32, device="cuda")
+            times = []
+            for _ in range(20):
+                with torch.cuda.stream(ts):
+                    flush.fill_(1.0)
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(ts)
+                prog.run_device(ins, out, st)
+                a1.record(ts)
+                st.synchronize()
+                times.append(a0.elapsed_time(a1))
+            cms = float(np.median(times))
+            ew["1024x1024_l2_flushed"] = {"ms": round(cms, 5), "GB/s": round(nbytes / cms / 1e6, 1),
+                                          "note": "median of 20 single calls after a 512 MB write"}
+            del flush, graph
         del ins, out, prog
     res["fused_elementwise"] = ew
     # reductions over X [8192, 4096] U(-1,1): sum/mean/max over axis 1, sum over axis 0 of X^T

@@ -206,6 +206,15 @@ int tt_event_create(void** event);
 int tt_event_destroy(void* event);
 int tt_event_record(void* event, void* stream);
 int tt_stream_wait_event(void* stream, void* event);
+/* CUDA graphs of queued work (no counterpart in the reference): everything queued on
+ * `stream` between begin and end — program runs in TT_DEVICE mode, SGD steps,
+ * all-reduces, and work on other streams joined through events — becomes one graph
+ * that tt_graph_launch replays with the same buffers.  For launch-bound loops (small
+ * programs called many times, a whole training step). */
+int tt_stream_begin_capture(void* stream);
+int tt_stream_end_capture(void* stream, void** graph_exec);
+int tt_graph_launch(void* graph_exec, void* stream);
+int tt_graph_destroy(void* graph_exec);
 
 /* ---- optimiser: SGD.step (python/tinytensor/optim.py:18-35) on device ----
  * For each i: v = momentum*v + g (when momentum > 0, velocities[i] != NULL);

@@ -172,6 +172,10 @@ SIGNATURES = {
     "tt_event_destroy": (ctypes.c_int, [_VP]),
     "tt_event_record": (ctypes.c_int, [_VP, _VP]),
     "tt_stream_wait_event": (ctypes.c_int, [_VP, _VP]),
+    "tt_stream_begin_capture": (ctypes.c_int, [_VP]),
+    "tt_stream_end_capture": (ctypes.c_int, [_VP, ctypes.POINTER(_VP)]),
+    "tt_graph_launch": (ctypes.c_int, [_VP, _VP]),
+    "tt_graph_destroy": (ctypes.c_int, [_VP]),
     "tt_sgd_step": (
         ctypes.c_int,
         [_I32, ctypes.POINTER(_VP), ctypes.POINTER(_VP), ctypes.POINTER(_VP), ctypes.POINTER(_I64), _F, _F, _VP],

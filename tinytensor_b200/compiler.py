@@ -8,6 +8,7 @@ and queues the work on a stream without synchronising (for chained programs, the
 training step and the benchmarks).
 """
 
+import contextlib
 import ctypes
 import os
 from collections.abc import Mapping, Sequence
@@ -19,7 +20,7 @@ from ._lib import RuntimeExecutionError, ShapeError, TypeError
 from .graph import Graph, Node
 
 __all__ = ["compile", "compile_gradients", "CompiledProgram", "gradients", "Tensor", "tensor",
-           "DeviceBuffer", "Stream", "Event", "launch_count"]
+           "DeviceBuffer", "Stream", "Event", "CudaGraph", "launch_count"]
 
 
 def _default_cache_dir():
@@ -101,6 +102,47 @@ class Event:
     def __del__(self):
         if getattr(self, "handle", None):
             _lib.lib.tt_event_destroy(self.handle)
+            self.handle = None
+
+
+class CudaGraph:
+    """Work queued on a stream, captured once and replayed (cudaGraph).
+
+        g = CudaGraph()
+        with g.capture(stream):
+            prog.run_device(ins, outs, stream)   # queued, not run
+        g.replay(stream)                        # runs it; repeat as often as needed
+
+    The captured work reads and writes the same buffers on every replay.  Run the
+    work once outside capture first (kernel attributes and modules are set up then).
+    """
+
+    def __init__(self):
+        self.handle = None
+
+    @contextlib.contextmanager
+    def capture(self, stream):
+        h = getattr(stream, "handle", stream)
+        _lib.check(_lib.lib.tt_stream_begin_capture(h))
+        ok = False
+        try:
+            yield self
+            ok = True
+        finally:
+            g = ctypes.c_void_p()
+            rc = _lib.lib.tt_stream_end_capture(h, ctypes.byref(g))
+            if ok:
+                _lib.check(rc)
+            if self.handle:
+                _lib.lib.tt_graph_destroy(self.handle)
+            self.handle = g.value
+
+    def replay(self, stream) -> None:
+        _lib.check(_lib.lib.tt_graph_launch(self.handle, getattr(stream, "handle", stream)))
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            _lib.lib.tt_graph_destroy(self.handle)
             self.handle = None
 
 

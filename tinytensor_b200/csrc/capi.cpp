@@ -484,6 +484,42 @@ int tt_stream_wait_event(void* stream, void* event) {
     });
 }
 
+int tt_stream_begin_capture(void* stream) {
+    return guarded([&] {
+        if (!stream) fail(TT_ERR_INVALID, "capture needs a created stream, not the legacy default stream");
+        check_cuda(cudaStreamBeginCapture(static_cast<cudaStream_t>(stream), cudaStreamCaptureModeThreadLocal),
+                   "cudaStreamBeginCapture");
+    });
+}
+
+int tt_stream_end_capture(void* stream, void** graph_exec) {
+    return guarded([&] {
+        if (!stream || !graph_exec) fail(TT_ERR_INVALID, "null argument");
+        *graph_exec = nullptr;
+        cudaGraph_t graph = nullptr;
+        check_cuda(cudaStreamEndCapture(static_cast<cudaStream_t>(stream), &graph), "cudaStreamEndCapture");
+        cudaGraphExec_t exec = nullptr;
+        cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        check_cuda(e, "cudaGraphInstantiate");
+        *graph_exec = exec;
+    });
+}
+
+int tt_graph_launch(void* graph_exec, void* stream) {
+    return guarded([&] {
+        if (!graph_exec) fail(TT_ERR_INVALID, "null graph");
+        check_cuda(cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph_exec), static_cast<cudaStream_t>(stream)),
+                   "cudaGraphLaunch");
+    });
+}
+
+int tt_graph_destroy(void* graph_exec) {
+    return guarded([&] {
+        if (graph_exec) check_cuda(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph_exec)), "cudaGraphExecDestroy");
+    });
+}
+
 int tt_program_status(tt_program* p, int32_t* device_status) {
     return guarded([&] {
         if (!p) fail(TT_ERR_INVALID, "null program");
