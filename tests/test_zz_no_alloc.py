@@ -40,7 +40,9 @@ def test_noalloc_gemm_matches_compiled_matmul_twice(m, n, k, tmp_path):
 
 def test_noalloc_gemm_rejects_products_beyond_its_scratch():
     tt.device_init(0)
-    m = n = k = 4096  # 2 * (m + n) * k floats of hi/lo copies: far above 32 MiB
+    # M <= 128 runs on single-CTA tiles, whose operands are split into hi/lo copies in
+    # scratch: 2 * (m + n) * k floats = 264 MB, far above the 32 MiB capacity
+    m, n, k = 128, 4096, 8192
     da, db, dc = tt.DeviceBuffer([m, k]), tt.DeviceBuffer([k, n]), tt.DeviceBuffer([m, n])
     with pytest.raises(tt.MemoryError, match="scratch"):
         _lib.check(_lib.lib.tt_gemm_f32_noalloc(da.ptr, db.ptr, dc.ptr, m, n, k, None, None))
