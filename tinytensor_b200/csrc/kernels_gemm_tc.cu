@@ -704,73 +704,53 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
     }
 }
 
-// M/N-contiguous view (s_r == 1) -> K-major hi/lo[b*l_b + r*l_r + k]: tiles of 32 K x 128
-// rows go through shared memory.  Loads run along r (float4 when vec4: R % 4 == 0, X,
-// s_k and s_b 16-B aligned), stores along k.  Shared rows hold 32 float4 chunks, chunk c
-// of row k at position c ^ (k & 7), so the float4 writes (one row per warp) and the
-// float4 reads (one row per lane) are both free of bank conflicts.
+// M/N-contiguous view (s_r == 1) -> K-major hi/lo[b*l_b + r*l_r + k], transposed in
+// registers: a thread loads a 4 (K) x 4 (rows) block as four float4s along the rows,
+// transposes it in registers and stores four float4s along K for hi and for lo.  A warp
+// covers 32 K x 16 rows (lane = 8 K-quads x 4 row-quads): loads are 64-B runs of 8 K-rows,
+// stores 128-B runs of 4 rows; no shared memory and no barriers.  vec4 (R % 4 == 0, X,
+// s_k and s_b 16-B aligned) allows the float4 loads; K-major rows are padded to
+// l_r >= round4(K), so a store may run into the padding (never read) but not past it.
 __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ X, float* __restrict__ hi,
                                                               float* __restrict__ lo, int64_t R, int64_t K,
                                                               int64_t s_k, int64_t s_b, int64_t l_r, int64_t l_b,
                                                               int vec4) {
-    __shared__ float4 th[32][32], tl[32][32];
     const int64_t b = blockIdx.y;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int q = lane & 7, c = lane >> 3;
     const float* xb = X + b * s_b;
     float* hb = hi + b * l_b;
     float* lb = lo + b * l_b;
-    const int64_t tk_n = (K + 31) / 32, tiles = tk_n * ((R + 127) / 128);
-    // the next tile's loads are issued before this tile's stores (software pipelining)
-    float v[4][4];
-    auto load = [&](int64_t t) {
+    const int64_t tk_n = (K + 31) / 32, tiles = tk_n * ((R + 15) / 16);
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * 8;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); t < tiles; t += warps) {
         const int64_t tr = t / tk_n;
-        const int64_t r0 = tr * 128, k0 = (t - tr * tk_n) * 32;
+        const int64_t k = (t - tr * tk_n) * 32 + 4 * q;   // this thread's 4 K values k..k+3
+        const int64_t r = tr * 16 + 4 * c;                 // and 4 rows r..r+3
+        float v[4][4];                                     // v[j][i] = X[k+j][r+i]
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const int64_t k = k0 + warp + 8 * j, r = r0 + 4 * lane;
-            if (vec4 && k < K && r < R) {
-                const float4 x = __ldg(reinterpret_cast<const float4*>(xb + k * s_k + r));
+            const float* src = xb + (k + j) * s_k + r;
+            if (vec4 && k + j < K && r < R) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(src));
                 v[j][0] = x.x; v[j][1] = x.y; v[j][2] = x.z; v[j][3] = x.w;
             } else {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) v[j][q] = (k < K && r + q < R) ? __ldg(xb + k * s_k + r + q) : 0.0f;
+                for (int i = 0; i < 4; ++i) v[j][i] = (k + j < K && r + i < R) ? __ldg(src + i) : 0.0f;
             }
         }
-    };
-    int64_t t = blockIdx.x;
-    if (t < tiles) load(t);
-    for (; t < tiles; t += gridDim.x) {
-        const int64_t tr = t / tk_n;
-        const int64_t r0 = tr * 128, k0 = (t - tr * tk_n) * 32;
+        if (k >= l_r) continue;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int kk = warp + 8 * j;
+        for (int i = 0; i < 4; ++i) {
+            if (r + i >= R) break;
             float4 h, l;
-            split_tf32(v[j][0], h.x, l.x);
-            split_tf32(v[j][1], h.y, l.y);
-            split_tf32(v[j][2], h.z, l.z);
-            split_tf32(v[j][3], h.w, l.w);
-            th[kk][lane ^ (kk & 7)] = h;
-            tl[kk][lane ^ (kk & 7)] = l;
+            split_tf32(v[0][i], h.x, l.x);
+            split_tf32(v[1][i], h.y, l.y);
+            split_tf32(v[2][i], h.z, l.z);
+            split_tf32(v[3][i], h.w, l.w);
+            *reinterpret_cast<float4*>(hb + (r + i) * l_r + k) = h;
+            *reinterpret_cast<float4*>(lb + (r + i) * l_r + k) = l;
         }
-        __syncthreads();
-        if (t + gridDim.x < tiles) load(t + gridDim.x);
-        const int64_t k = k0 + lane;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int c = warp + 8 * j;
-            const float4 h = th[lane][c ^ (lane & 7)], l = tl[lane][c ^ (lane & 7)];
-            const float hv[4] = {h.x, h.y, h.z, h.w}, lv[4] = {l.x, l.y, l.z, l.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int64_t r = r0 + 4 * c + q;
-                if (r < R && k < K) {
-                    hb[r * l_r + k] = hv[q];
-                    lb[r * l_r + k] = lv[q];
-                }
-            }
-        }
-        __syncthreads();
     }
 }
 
@@ -798,13 +778,13 @@ int launch_split(const float* X, float* hi, float* lo, int64_t R, int64_t K, int
     const bool x16 = (reinterpret_cast<uintptr_t>(X) & 15) == 0 && (o.nb == 1 || s_b % 4 == 0);
     if (s_r == 1 && s_k != 1 && R > 1 && K > 1) {
         const bool vec4 = x16 && R % 4 == 0 && s_k % 4 == 0;
-        // one resident wave of grid-stride CTAs
+        // one resident wave of grid-stride CTAs (8 warps each, a 32 x 16 tile per warp)
         static const int per_sm = [] {
             int n = 0;
             if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, split_transpose_kernel, 256, 0) != cudaSuccess) n = 4;
             return n > 0 ? n : 1;
         }();
-        int64_t blocks = ((R + 127) / 128) * ((K + 31) / 32);
+        int64_t blocks = (((R + 15) / 16) * ((K + 31) / 32) + 7) / 8;
         if (blocks > 148 * per_sm) blocks = 148 * per_sm;
         split_transpose_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(o.nb)), 256, 0, st>>>(
             X, hi, lo, R, K, s_k, s_b, o.lr, o.lb, vec4 ? 1 : 0);
