@@ -126,6 +126,9 @@ typedef struct tt_compile_options {
 #define TT_FLAG_NO_GEMM_FUSION 2  /* keep GEMM epilogues plain (diagnostics) */
 #define TT_FLAG_HOST_ONLY 4       /* plan + generate + NVRTC-compile only: no device, no arena
                                      (tt_program_info works; tt_program_run reports no device) */
+#define TT_FLAG_SERIAL 8          /* every launch on the run's stream, one after another (by
+                                     default two adjacent independent GEMMs run side by side
+                                     on a second stream of the program) */
 
 typedef struct tt_program tt_program;
 

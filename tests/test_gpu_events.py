@@ -87,3 +87,32 @@ def test_step_host_matches_device_steps(cache_dir):
         results.append([p.numpy() for p in params])
     for a, b in zip(*results):
         assert np.array_equal(a, b)
+
+
+def test_concurrent_gemm_pairs_match_serial_program(cache_dir):
+    """The same gradient program with its independent GEMM pairs on two streams and with
+    TT_FLAG_SERIAL gives bit-identical outputs (same kernels, same data)."""
+    rows, dims = 1024, (256, 512, 512, 10)
+    rng = np.random.default_rng(17)
+    g = tt.Graph()
+    X, T = g.input([rows, dims[0]]), g.input([rows, dims[3]])
+    W = [g.input([a, b]) for a, b in zip(dims[:-1], dims[1:])]
+    d = tt.tanh(tt.relu(X @ W[0]) @ W[1]) @ W[2] - T
+    loss = tt.mean(d * d)
+    feeds = [rng.standard_normal((rows, dims[0])).astype(np.float32),
+             rng.standard_normal((rows, dims[3])).astype(np.float32)]
+    feeds += [(rng.standard_normal((a, b)) / np.sqrt(a)).astype(np.float32) for a, b in zip(dims[:-1], dims[1:])]
+    results = []
+    for flags in (0, tt.FLAG_SERIAL):
+        prog = tt.compile_gradients(g, loss, W, cache_dir=cache_dir, flags=flags)
+        assert ("runs beside" in prog.execution_plan()) == (flags == 0)
+        ins = [tt.DeviceBuffer.from_numpy(a) for a in feeds]
+        outs = [tt.DeviceBuffer([])] + [tt.DeviceBuffer(w.shape) for w in feeds[2:]]
+        stream = tt.Stream()
+        for _ in range(3):
+            prog.run_device(ins, outs, stream)
+        stream.synchronize()
+        assert prog.status() == 0
+        results.append([o.numpy() for o in outs])
+    for a, b in zip(*results):
+        assert np.array_equal(a, b)

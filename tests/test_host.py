@@ -261,3 +261,41 @@ def test_gradients_are_scheduled_early_with_output_steps(cache_dir):
     assert dw3_s < dw2_s < dw1_s
     dh1 = [i for i, l in enumerate(launches) if "[64x256x256" in l and "B:K" in l]
     assert dh1 and dw2_s < dh1[0]
+
+
+def test_independent_gemms_run_side_by_side_without_sharing_memory(cache_dir):
+    """dW2 and dH1 of the MLP backward are adjacent, independent GEMMs: they are marked to
+    run on two streams, and none of their buffers overlap in the arena.  TT_FLAG_SERIAL
+    keeps every launch on one stream."""
+    rows = 512
+    g = tt.Graph()
+    X, T = g.input([rows, 256]), g.input([rows, 10])
+    W1, W2, W3 = g.input([256, 512]), g.input([512, 512]), g.input([512, 10])
+    d = tt.tanh(tt.relu(X @ W1) @ W2) @ W3 - T
+    loss = tt.mean(d * d)
+    p = tt.compile_gradients(g, loss, [W1, W2, W3], cache_dir=cache_dir, flags=HOST)
+    lines = [line.strip() for line in p.execution_plan().splitlines() if line.strip().startswith("[")]
+    pairs = [i for i, line in enumerate(lines) if "runs beside" in line]
+    assert pairs
+    sizes = {}
+    for i in pairs:
+        a, b = lines[i], lines[i + 1]
+        assert "gemm/" in a and "gemm/" in b
+
+        def spans(line):
+            out = []
+            m = re.search(r"-> arena:(\d+)", line)
+            shape = re.search(r"\[(\d+)x(\d+)x(\d+)", line)
+            if m and shape:
+                out.append((int(m.group(1)), int(shape.group(1)) * int(shape.group(2)) * 4))
+            s = re.search(r"scratch=(\d+)@(\d+)", line)
+            if s:
+                out.append((int(s.group(2)), int(s.group(1))))
+            return out
+
+        for (o1, n1) in spans(a):
+            for (o2, n2) in spans(b):
+                assert o1 + n1 <= o2 or o2 + n2 <= o1, (a, b)
+        sizes[i] = (a, b)
+    serial = tt.compile_gradients(g, loss, [W1, W2, W3], cache_dir=cache_dir, flags=HOST | tt.FLAG_SERIAL)
+    assert "runs beside" not in serial.execution_plan()

@@ -101,10 +101,15 @@ struct tt_program {
     bool prof_pending = false;
     bool has_tc = false;
     std::vector<cudaEvent_t> out_events;  // caller's events, recorded when an output is complete
+    cudaStream_t side = nullptr;          // second stream for concurrent GEMM pairs
+    cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     std::mutex run_mutex;
 
     ~tt_program() {
         for (cudaEvent_t e : events) cudaEventDestroy(e);
+        if (fork_ev) cudaEventDestroy(fork_ev);
+        if (join_ev) cudaEventDestroy(join_ev);
+        if (side) cudaStreamDestroy(side);
         if (mod.module) driver().moduleUnload(mod.module);
         if (arena) cudaFree(arena);
     }
@@ -207,6 +212,7 @@ int tt_compile(const tt_graph* cg, const tt_compile_options* opt, tt_program** o
         ScheduleOptions so;
         so.fuse = !(o.flags & TT_FLAG_NO_FUSION);
         so.gemm_epilogue = !(o.flags & TT_FLAG_NO_GEMM_FUSION);
+        so.concurrent_gemms = !(o.flags & TT_FLAG_SERIAL);
         p->plan = schedule(g, so);
         p->source = generate_source(p->plan);
         for (int k : p->plan.g.inputs) {
@@ -256,6 +262,13 @@ int tt_compile(const tt_graph* cg, const tt_compile_options* opt, tt_program** o
                        "constant upload");
         }
         check_cuda(cudaMemset(p->arena + p->plan.status_offset, 0, 256), "status word init");
+        bool pairs = false;
+        for (const Launch& L : p->plan.launches) pairs |= L.concurrent_next;
+        if (pairs) {
+            check_cuda(cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking), "cudaStreamCreate(side)");
+            check_cuda(cudaEventCreateWithFlags(&p->fork_ev, cudaEventDisableTiming), "cudaEventCreate(fork)");
+            check_cuda(cudaEventCreateWithFlags(&p->join_ev, cudaEventDisableTiming), "cudaEventCreate(join)");
+        }
         *out = p.release();
     });
 }
@@ -307,23 +320,23 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
         }
     };
     int* status = reinterpret_cast<int*>(p->arena + pl.status_offset);
+    const size_t n = pl.launches.size();
     if (p->profiling) {
-        size_t need = pl.launches.size() + 1;
-        while (p->events.size() < need) {
+        // start and end event per launch (launches of a concurrent pair overlap)
+        while (p->events.size() < 2 * n) {
             cudaEvent_t e;
             check_cuda(cudaEventCreate(&e), "cudaEventCreate");
             p->events.push_back(e);
         }
-        check_cuda(cudaEventRecord(p->events[0], stream), "cudaEventRecord");
     }
-    auto record_outputs = [&](int step) {
+    auto record_outputs = [&](int step, cudaStream_t st) {
         for (size_t k = 0; k < p->out_events.size(); ++k)
             if (p->out_events[k] && pl.output_step[k] == step)
-                check_cuda(cudaEventRecord(p->out_events[k], stream), "cudaEventRecord(output)");
+                check_cuda(cudaEventRecord(p->out_events[k], st), "cudaEventRecord(output)");
     };
-    record_outputs(-1);
-    for (size_t s = 0; s < pl.launches.size(); ++s) {
+    auto launch_one = [&](size_t s, cudaStream_t st) {
         const Launch& L = pl.launches[s];
+        if (p->profiling) check_cuda(cudaEventRecord(p->events[2 * s], st), "cudaEventRecord");
         int rc = 0;
         if (L.type == LT_REGION) {
             const Region& r = pl.regions[static_cast<size_t>(L.region)];
@@ -337,22 +350,38 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
                 std::vector<void*> args;
                 for (void*& v : vals) args.push_back(&v);
                 CUresult cr = driver().launchKernel(p->region_fn[static_cast<size_t>(L.region)],
-                                                    static_cast<unsigned>(r.grid), 1, 1, 256, 1, 1, 0, stream,
+                                                    static_cast<unsigned>(r.grid), 1, 1, 256, 1, 1, 0, st,
                                                     args.data(), nullptr);
                 if (cr != CUDA_SUCCESS) fail(TT_ERR_RUNTIME, "cuLaunchKernel(" + r.kernel + "): " + cu_error(cr));
             }
         } else if (L.type == LT_REDUCE) {
             rc = launch_reduce(L.rd, reinterpret_cast<const float*>(resolve(L.in_ref)),
-                               reinterpret_cast<float*>(resolve(L.out_ref)), resolve(L.scratch_ref), stream);
+                               reinterpret_cast<float*>(resolve(L.out_ref)), resolve(L.scratch_ref), st);
         } else {
             rc = launch_gemm(L.gd, reinterpret_cast<const float*>(resolve(L.in_ref)),
                              reinterpret_cast<const float*>(resolve(L.in_ref2)),
-                             reinterpret_cast<float*>(resolve(L.out_ref)), resolve(L.scratch_ref), status, stream);
+                             reinterpret_cast<float*>(resolve(L.out_ref)), resolve(L.scratch_ref), status, st);
         }
         if (rc) fail(TT_ERR_RUNTIME, L.label + ": " + cudaGetErrorString(static_cast<cudaError_t>(rc)));
         g_launches += static_cast<uint64_t>(launches_of(pl, L));
-        if (p->profiling) check_cuda(cudaEventRecord(p->events[s + 1], stream), "cudaEventRecord");
-        record_outputs(static_cast<int>(s));
+        if (p->profiling) check_cuda(cudaEventRecord(p->events[2 * s + 1], st), "cudaEventRecord");
+        record_outputs(static_cast<int>(s), st);
+    };
+    record_outputs(-1, stream);
+    for (size_t s = 0; s < n; ++s) {
+        if (pl.launches[s].concurrent_next && p->side) {
+            // fork: the side stream starts after everything queued so far; join: the run's
+            // stream continues after both
+            check_cuda(cudaEventRecord(p->fork_ev, stream), "cudaEventRecord(fork)");
+            check_cuda(cudaStreamWaitEvent(p->side, p->fork_ev, 0), "cudaStreamWaitEvent(fork)");
+            launch_one(s, stream);
+            launch_one(s + 1, p->side);
+            check_cuda(cudaEventRecord(p->join_ev, p->side), "cudaEventRecord(join)");
+            check_cuda(cudaStreamWaitEvent(stream, p->join_ev, 0), "cudaStreamWaitEvent(join)");
+            ++s;
+        } else {
+            launch_one(s, stream);
+        }
     }
     p->prof_pending = p->profiling;
 }
@@ -362,11 +391,12 @@ static void collect_profile(tt_program* p) {
     if (!p->prof_pending) return;
     p->prof_pending = false;
     const size_t n = p->plan.launches.size();
-    check_cuda(cudaEventSynchronize(p->events[n]), "profile event");
+    if (n == 0) return;
+    for (size_t s = 0; s < n; ++s) check_cuda(cudaEventSynchronize(p->events[2 * s + 1]), "profile event");
     if (p->prof_sum.size() != n) p->prof_sum.assign(n, 0.0);
     for (size_t s = 0; s < n; ++s) {
         float ms = 0.f;
-        check_cuda(cudaEventElapsedTime(&ms, p->events[s], p->events[s + 1]), "cudaEventElapsedTime");
+        check_cuda(cudaEventElapsedTime(&ms, p->events[2 * s], p->events[2 * s + 1]), "cudaEventElapsedTime");
         p->prof_sum[s] += ms;
     }
     p->prof_runs++;

@@ -650,8 +650,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ P, float* __restrict__ C,
                                                             int64_t per, int ksplit, int64_t c_bstride, int epilogue) {
     const int64_t b = blockIdx.y;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < per;
-         i += static_cast<int64_t>(gridDim.x) * 256) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * 256;
+    const bool vec = (per % 4 == 0) && (c_bstride % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+    if (vec) {
+        // float4 per thread; the ksplit loads of one float4 are independent (in flight together)
+        for (int64_t i = (static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x) * 4; i < per; i += stride * 4) {
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int s = 0; s < ksplit; ++s) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(P + (b * ksplit + s) * per + i));
+                v.x = __fadd_rn(v.x, x.x);
+                v.y = __fadd_rn(v.y, x.y);
+                v.z = __fadd_rn(v.z, x.z);
+                v.w = __fadd_rn(v.w, x.w);
+            }
+            if (epilogue == EP_RELU) {
+                v.x = v.x > 0.0f ? v.x : 0.0f;
+                v.y = v.y > 0.0f ? v.y : 0.0f;
+                v.z = v.z > 0.0f ? v.z : 0.0f;
+                v.w = v.w > 0.0f ? v.w : 0.0f;
+            }
+            *reinterpret_cast<float4*>(C + b * c_bstride + i) = v;
+        }
+        return;
+    }
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < per; i += stride) {
         float v = 0.0f;
         for (int s = 0; s < ksplit; ++s) v = __fadd_rn(v, __ldg(P + (b * ksplit + s) * per + i));
         if (epilogue == EP_RELU) v = v > 0.0f ? v : 0.0f;
@@ -977,6 +1000,10 @@ int launch_splitk_reduce(const float* P, float* C, int64_t per, int ksplit, int6
     splitk_reduce_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(batch)), 256, 0,
                            static_cast<cudaStream_t>(stream)>>>(P, C, per, ksplit, c_sb, epilogue);
     return static_cast<int>(cudaGetLastError());
+}
+
+int64_t gemm_tc_ctas(const GemmDesc& d) {
+    return d.algo == 2 ? ctas_of(d) * d.ksplit : 0;
 }
 
 int gemm_tc_launch_count(const GemmDesc& d) {

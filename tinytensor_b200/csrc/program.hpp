@@ -60,6 +60,7 @@ void plan_gemm(GemmDesc& d);  // picks the kernel variant for the shape/layout
 const char* gemm_algo_name(int algo);
 int64_t gemm_scratch_bytes(const GemmDesc& d);  // device scratch the chosen variant needs
 int gemm_launch_count(const GemmDesc& d);        // kernels one launch_gemm issues
+int64_t gemm_tc_ctas(const GemmDesc& d);         // CTAs of a tensor-core GEMM's main kernel (0 otherwise)
 int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
                 void* stream);
 // Sums split-K partials P[b][s][0..per) in split order into C[b*c_sb + i] and applies
@@ -106,6 +107,7 @@ struct Launch {
     BufRef in_ref, in_ref2, out_ref, scratch_ref;
     int64_t scratch_bytes = 0;
     std::string label;                  // for profiles and the execution plan
+    bool concurrent_next = false;       // this GEMM and the next launch (a GEMM) run side by side
 };
 
 struct Slot {

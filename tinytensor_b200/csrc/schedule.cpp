@@ -669,10 +669,44 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         p.launches.push_back(L);
     }
 
+    // ---- concurrent GEMM pairs ----
+    // Two adjacent tensor-core GEMM launches, the second neither reading the first's
+    // output nor writing what the first reads, each of at most four waves of CTAs, run
+    // side by side on two streams: the CTAs of one fill the part-empty last wave of the
+    // other.  Measured on B200 for the MLP gradient program: 2 % faster with 4096-row
+    // shards (two 512-CTA GEMMs), equal at 8192 rows, 7 % slower at 32768 rows (two big
+    // GEMMs interleaved thrash each other's L2 working set) -- hence the size limit.  For
+    // the memory plan a pair is one step, so none of their buffers or scratch share a slot.
+    const size_t nl = p.launches.size();
+    std::vector<int> plan_step(nl + 1, 0);
+    {
+        int stp = 0;
+        for (size_t s = 0; s < nl; ++s) {
+            plan_step[s] = stp;
+            const int64_t wave4 = 4 * 148;
+            if (opt.concurrent_gemms && s + 1 < nl && p.launches[s].type == LT_GEMM &&
+                p.launches[s + 1].type == LT_GEMM && gemm_tc_ctas(p.launches[s].gd) > 0 &&
+                gemm_tc_ctas(p.launches[s].gd) <= wave4 && gemm_tc_ctas(p.launches[s + 1].gd) > 0 &&
+                gemm_tc_ctas(p.launches[s + 1].gd) <= wave4) {
+                const Launch& a = p.launches[s];
+                const Launch& b = p.launches[s + 1];
+                const bool dep = b.in_node == a.out_node || b.in_node2 == a.out_node || a.in_node == b.out_node ||
+                                 a.in_node2 == b.out_node || a.out_node == b.out_node;
+                if (!dep) {
+                    p.launches[s].concurrent_next = true;
+                    plan_step[s + 1] = stp;
+                    ++s;
+                }
+            }
+            ++stp;
+        }
+        plan_step[nl] = stp;
+    }
+
     // ---- 4. memory plan ----
     // Roots needing arena slots: computed roots not bound to an output buffer.
     std::vector<int> step_of_unit(units.size());
-    for (size_t s = 0; s < order.size(); ++s) step_of_unit[static_cast<size_t>(order[s])] = static_cast<int>(s);
+    for (size_t s = 0; s < order.size(); ++s) step_of_unit[static_cast<size_t>(order[s])] = plan_step[s];
     struct Life {
         int root;  // node, or -1 - launch index for scratch
         int first, last;
@@ -696,8 +730,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         }
     for (size_t s = 0; s < p.launches.size(); ++s)
         if (p.launches[s].scratch_bytes > 0)
-            lives.push_back(Life{-1 - static_cast<int>(s), static_cast<int>(s), static_cast<int>(s),
-                                 p.launches[s].scratch_bytes});
+            lives.push_back(Life{-1 - static_cast<int>(s), plan_step[s], plan_step[s], p.launches[s].scratch_bytes});
     p.num_intermediates = lives.size();
     for (const Life& l : lives) p.total_alloc_bytes += l.bytes;
     for (size_t s = 0; s <= p.launches.size(); ++s) {
@@ -826,6 +859,7 @@ std::string plan_text(const Plan& p) {
                << (L.out_ref.kind == BK_ARENA ? L.out_ref.offset : L.out_ref.index);
             if (L.scratch_bytes) ss << " scratch=" << L.scratch_bytes << "@" << L.scratch_ref.offset;
         }
+        if (L.concurrent_next) ss << "  || runs beside [" << s + 1 << "] on the second stream";
         ss << "\n";
     }
     return ss.str();

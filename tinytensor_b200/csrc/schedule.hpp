@@ -44,6 +44,7 @@ struct Plan {
 struct ScheduleOptions {
     bool fuse = true;
     bool gemm_epilogue = true;
+    bool concurrent_gemms = true;
 };
 
 Plan schedule(const Graph& g, const ScheduleOptions& opt);
