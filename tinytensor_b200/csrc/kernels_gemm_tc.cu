@@ -696,33 +696,46 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     }
 }
 
-// View X[b][r][k] = X[b*s_b + r*s_r + k*s_k] -> hi/lo[b*l_b + r*l_r + k], one warp per
-// row r.  vec4 (s_k == 1, K % 4 == 0, X, s_r and s_b 16-B aligned) moves float4s.
+// View X[b][r][k] = X[b*s_b + r*s_r + k*s_k] -> hi/lo[b*l_b + r*l_r + k].  Work units
+// are 1024-float segments of a row, one warp per unit (so a few long rows still spread
+// over the whole GPU); the vec4 path (s_k == 1, K % 4 == 0, X, s_r and s_b 16-B
+// aligned) issues a lane's eight float4 loads before its stores, 4 KB in flight per warp.
 __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ X, float* __restrict__ hi,
                                                          float* __restrict__ lo, int64_t R, int64_t K, int64_t s_r,
                                                          int64_t s_k, int64_t s_b, int64_t l_r, int64_t l_b,
                                                          int vec4) {
+    constexpr int SEG = 1024;
     const int64_t b = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float* xb = X + b * s_b;
-    for (int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp; r < R; r += static_cast<int64_t>(gridDim.x) * 8) {
+    const int64_t segs = (K + SEG - 1) / SEG;
+    for (int64_t u = static_cast<int64_t>(blockIdx.x) * 8 + warp; u < R * segs; u += static_cast<int64_t>(gridDim.x) * 8) {
+        const int64_t r = u / segs, k0 = (u - r * segs) * SEG;
+        const int64_t k1 = k0 + SEG < K ? k0 + SEG : K;
         const float* xr = xb + r * s_r;
         float* hr = hi + b * l_b + r * l_r;
         float* lr = lo + b * l_b + r * l_r;
         if (vec4) {
-#pragma unroll 4
-            for (int64_t i = lane * 4; i < K; i += 128) {
-                const float4 x = __ldg(reinterpret_cast<const float4*>(xr + i));
+            float4 x[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int64_t i = k0 + lane * 4 + 128 * j;
+                x[j] = i < k1 ? __ldg(reinterpret_cast<const float4*>(xr + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int64_t i = k0 + lane * 4 + 128 * j;
+                if (i >= k1) break;
                 float4 h, l;
-                split_tf32(x.x, h.x, l.x);
-                split_tf32(x.y, h.y, l.y);
-                split_tf32(x.z, h.z, l.z);
-                split_tf32(x.w, h.w, l.w);
+                split_tf32(x[j].x, h.x, l.x);
+                split_tf32(x[j].y, h.y, l.y);
+                split_tf32(x[j].z, h.z, l.z);
+                split_tf32(x[j].w, h.w, l.w);
                 *reinterpret_cast<float4*>(hr + i) = h;
                 *reinterpret_cast<float4*>(lr + i) = l;
             }
         } else {
-            for (int64_t i = lane; i < K; i += 32) split_tf32(__ldg(xr + i * s_k), hr[i], lr[i]);
+            for (int64_t i = k0 + lane; i < k1; i += 32) split_tf32(__ldg(xr + i * s_k), hr[i], lr[i]);
         }
     }
 }
@@ -814,8 +827,13 @@ int launch_split(const float* X, float* hi, float* lo, int64_t R, int64_t K, int
         return static_cast<int>(cudaGetLastError());
     }
     const bool vec4 = x16 && (s_k == 1 || K == 1) && K % 4 == 0 && s_r % 4 == 0;
-    int64_t blocks = (R + 7) / 8;
-    if (blocks > 148 * 16) blocks = 148 * 16;
+    static const int rows_per_sm = [] {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, split_rows_kernel, 256, 0) != cudaSuccess) n = 4;
+        return n > 0 ? n : 1;
+    }();
+    int64_t blocks = (R * ((K + 1023) / 1024) + 7) / 8;
+    if (blocks > 148 * rows_per_sm) blocks = 148 * rows_per_sm;
     split_rows_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(o.nb)), 256, 0, st>>>(
         X, hi, lo, R, K, s_r, s_k, s_b, o.lr, o.lb, vec4 ? 1 : 0);
     return static_cast<int>(cudaGetLastError());
