@@ -219,6 +219,14 @@ int tt_stream_end_capture(void* stream, void** graph_exec);
 int tt_graph_launch(void* graph_exec, void* stream);
 int tt_graph_destroy(void* graph_exec);
 
+/* ---- diagnostics (no counterpart in the reference) ----
+ * Runs one CTA that waits on an mbarrier nothing arrives at, through the same bounded
+ * wait every tensor-core GEMM wait uses, with a budget of `budget_cycles` SM clock
+ * cycles (at most 4e9), then synchronises.  *status_out receives the code the wait
+ * records on giving up (0x200 = a timed-out data wait); the context stays usable.  Shows
+ * that a missing arrival ends in a status the host reads, not in a hang. */
+int tt_selftest_bounded_wait(int64_t budget_cycles, int32_t* status_out);
+
 /* ---- optimiser: SGD.step (python/tinytensor/optim.py:18-35) on device ----
  * For each i: v = momentum*v + g (when momentum > 0, velocities[i] != NULL);
  * p -= lr * (momentum > 0 ? v : g).  One fused launch over all parameters. */

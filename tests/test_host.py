@@ -299,3 +299,10 @@ def test_independent_gemms_run_side_by_side_without_sharing_memory(cache_dir):
         sizes[i] = (a, b)
     serial = tt.compile_gradients(g, loss, [W1, W2, W3], cache_dir=cache_dir, flags=HOST | tt.FLAG_SERIAL)
     assert "runs beside" not in serial.execution_plan()
+
+
+def test_bounded_wait_selftest_rejects_unbounded_budgets():
+    import ctypes
+    status = ctypes.c_int32(0)
+    with pytest.raises(ValueError):
+        _lib.check(_lib.lib.tt_selftest_bounded_wait(10**12, ctypes.byref(status)))

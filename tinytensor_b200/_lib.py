@@ -172,6 +172,7 @@ SIGNATURES = {
     "tt_event_destroy": (ctypes.c_int, [_VP]),
     "tt_event_record": (ctypes.c_int, [_VP, _VP]),
     "tt_stream_wait_event": (ctypes.c_int, [_VP, _VP]),
+    "tt_selftest_bounded_wait": (ctypes.c_int, [_I64, ctypes.POINTER(_I32)]),
     "tt_stream_begin_capture": (ctypes.c_int, [_VP]),
     "tt_stream_end_capture": (ctypes.c_int, [_VP, ctypes.POINTER(_VP)]),
     "tt_graph_launch": (ctypes.c_int, [_VP, _VP]),

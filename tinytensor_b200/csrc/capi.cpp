@@ -514,6 +514,23 @@ int tt_stream_wait_event(void* stream, void* event) {
     });
 }
 
+int tt_selftest_bounded_wait(int64_t budget_cycles, int32_t* status_out) {
+    return guarded([&] {
+        if (!status_out) fail(TT_ERR_INVALID, "null argument");
+        if (budget_cycles < 0 || budget_cycles > 4000000000LL) fail(TT_ERR_INVALID, "budget must be 0..4e9 cycles");
+        int* d = nullptr;
+        check_cuda(cudaMalloc(reinterpret_cast<void**>(&d), sizeof(int)), "cudaMalloc(status)");
+        cudaError_t e = cudaMemset(d, 0, sizeof(int));
+        if (e == cudaSuccess) e = static_cast<cudaError_t>(launch_bounded_wait_selftest(d, budget_cycles, nullptr));
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        int32_t v = 0;
+        if (e == cudaSuccess) e = cudaMemcpy(&v, d, sizeof(int), cudaMemcpyDeviceToHost);
+        cudaFree(d);
+        check_cuda(e, "bounded-wait self-test");
+        *status_out = v;
+    });
+}
+
 int tt_stream_begin_capture(void* stream) {
     return guarded([&] {
         if (!stream) fail(TT_ERR_INVALID, "capture needs a created stream, not the legacy default stream");

@@ -117,7 +117,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait: false if the phase does not complete within the clock budget, if this
 // CTA has aborted, or if another CTA has already reported a timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
-                                          int code) {
+                                          int code, long long budget = WAIT_BUDGET) {
     const long long t0 = clock64();
     uint32_t polls = 0;
     while (!mbar_try_wait(bar, parity)) {
@@ -126,7 +126,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
             *abort_flag = 1;
             return false;
         }
-        if (clock64() - t0 > WAIT_BUDGET) {
+        if (clock64() - t0 > budget) {
             *abort_flag = 1;
             atomicCAS(status, 0, code);
             return false;
@@ -1009,6 +1009,29 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
     }
     if (rc || d.ksplit == 1) return rc;
     return launch_splitk_reduce(partial, C, d.M * d.N, d.ksplit, d.batch, d.c_sb, d.epilogue, st);
+}
+
+namespace {
+// A barrier that nothing arrives at: the GEMM kernels' bounded wait must give up after
+// `budget` cycles, raise the abort flag, record ST_TIMEOUT_FULL in the status word and
+// return, leaving the context usable.
+__global__ void bounded_wait_selftest_kernel(int* status, long long budget) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, status, ST_TIMEOUT_FULL, budget);
+    __syncthreads();
+}
+}  // namespace
+
+int launch_bounded_wait_selftest(int* status, long long budget, void* stream) {
+    bounded_wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, budget);
+    return static_cast<int>(cudaGetLastError());
 }
 
 int launch_splitk_reduce(const float* P, float* C, int64_t per, int ksplit, int64_t batch, int64_t c_sb, int epilogue,

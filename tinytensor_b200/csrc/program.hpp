@@ -68,6 +68,10 @@ int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, voi
 int launch_splitk_reduce(const float* P, float* C, int64_t per, int ksplit, int64_t batch, int64_t c_sb, int epilogue,
                          void* stream);
 
+// Diagnostic: one CTA waits on an mbarrier nothing arrives at, with the GEMM kernels'
+// bounded wait and the given clock budget; the wait records its timeout code in *status.
+int launch_bounded_wait_selftest(int* status, long long budget, void* stream);
+
 // ---- misc kernels (kernels_misc.cu) ----
 int launch_sgd(int n, float* const* params, const float* const* grads, float* const* vel, const int64_t* numels,
                float lr, float momentum, void* stream);
