@@ -23,6 +23,18 @@ __all__ = ["compile", "compile_gradients", "CompiledProgram", "gradients", "Tens
            "DeviceBuffer", "Stream", "Event", "CudaGraph", "launch_count"]
 
 
+def _release(fn_name, handle):
+    """Frees a native handle from a destructor.  At interpreter exit the module globals
+    may already be gone (then the process teardown frees everything anyway)."""
+    lib = getattr(_lib, "lib", None)
+    if lib is None or not handle:
+        return
+    try:
+        getattr(lib, fn_name)(handle)
+    except Exception:
+        pass
+
+
 def _default_cache_dir():
     return os.environ.get("TT_CUDA_CACHE", os.path.join(os.path.expanduser("~"), ".cache", "tinytensor_b200"))
 
@@ -80,7 +92,7 @@ class Stream:
 
     def __del__(self):
         if getattr(self, "_own", False) and self.handle:
-            _lib.lib.tt_stream_destroy(self.handle)
+            _release("tt_stream_destroy", self.handle)
             self.handle = None
 
 
@@ -101,7 +113,7 @@ class Event:
 
     def __del__(self):
         if getattr(self, "handle", None):
-            _lib.lib.tt_event_destroy(self.handle)
+            _release("tt_event_destroy", self.handle)
             self.handle = None
 
 
@@ -142,7 +154,7 @@ class CudaGraph:
 
     def __del__(self):
         if getattr(self, "handle", None):
-            _lib.lib.tt_graph_destroy(self.handle)
+            _release("tt_graph_destroy", self.handle)
             self.handle = None
 
 
@@ -204,7 +216,7 @@ class PinnedBuffer:
 
     def __del__(self):
         if getattr(self, "ptr", None):
-            _lib.lib.tt_host_free(self.ptr)
+            _release("tt_host_free", self.ptr)
             self.ptr = None
 
 
@@ -235,7 +247,7 @@ class CompiledProgram:
     def __del__(self):
         h = getattr(self, "_h", None)
         if h:
-            _lib.lib.tt_program_destroy(h)
+            _release("tt_program_destroy", h)
             self._h = None
 
     # -- diagnostics (Executor::original_ir etc.) -----------------------------------------
