@@ -81,6 +81,7 @@ struct TcParams {
     int M, N, K;
     int a_batched, b_batched;
     int ksplit, kb_per_split, chunk_kb;
+    int tiles_m, tiles_n, n_units;  // pair kernel: 256x256 tiles and work units (tiles x batch x splits)
     int epilogue;        // applied here only when ksplit == 1
     int* status;
 };
@@ -462,6 +463,33 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
 constexpr uint32_t kIdescPair = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(256 >> 3) << 17) |
                                 (static_cast<uint32_t>(256 >> 4) << 24);
 
+// Work unit u of the persistent pair kernel: output pair-tile (tm, tn) of batch/split zz.
+// N-tiles vary fastest, so the clusters running at the same time share A row tiles.
+struct PairUnit {
+    int n0, m0, nb0, zb_all, za, zb, kb0, kcount;
+};
+
+__device__ __forceinline__ PairUnit pair_unit(const TcParams& p, int u, uint32_t rank, int nkb_total) {
+    PairUnit w;
+    const int per_z = p.tiles_m * p.tiles_n;
+    const int zz = u / per_z, rem = u - zz * per_z;
+    const int tm = rem / p.tiles_n, tn = rem - tm * p.tiles_n;
+    w.n0 = tn * 256;
+    w.m0 = tm * 256 + static_cast<int>(rank) * 128;
+    w.nb0 = w.n0 + static_cast<int>(rank) * 128;
+    w.zb_all = zz;
+    const int batch = zz / p.ksplit, split = zz - batch * p.ksplit;
+    w.za = p.a_batched ? batch : 0;
+    w.zb = p.b_batched ? batch : 0;
+    w.kb0 = split * p.kb_per_split;
+    w.kcount = max(0, min(nkb_total, w.kb0 + p.kb_per_split) - w.kb0);
+    return w;
+}
+
+// Persistent: each cluster walks the units u = cluster, cluster + clusters, ...  The
+// stage ring, the TMEM chunk double buffer and every barrier phase run on counters
+// that continue across units, so the epilogue of one tile (its last drain and its
+// stores) overlaps the TMA loads and MMAs of the next.
 template <int BK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
@@ -482,16 +510,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = (blockIdx.x >> 1) * 256;                 // pair's N range [n0, n0 + 256)
-    const int m0 = blockIdx.y * 256 + static_cast<int>(rank) * 128;  // this CTA's A rows / output rows
-    const int nb0 = n0 + static_cast<int>(rank) * 128;      // this CTA's half of B
-    const int zb_all = blockIdx.z;
-    const int batch = zb_all / p.ksplit, split = zb_all - batch * p.ksplit;
-    const int za = p.a_batched ? batch : 0, zb = p.b_batched ? batch : 0;
+    const int cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
     const int nkb_total = (p.K + BK - 1) / BK;
-    const int kb0 = split * p.kb_per_split;
-    const int kcount = max(0, min(nkb_total, kb0 + p.kb_per_split) - kb0);
-    const int nchunks = (kcount + p.chunk_kb - 1) / p.chunk_kb;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -519,25 +539,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_ahi)) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_bhi)) : "memory");
-            int issued = 0;
-            for (int i = 0; i < kcount; ++i) {
-                const int s = i % STAGES;
-                const uint32_t ph = (i / STAGES) & 1;
-                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ST_TIMEOUT_EMPTY)) break;
-                uint8_t* st = tiles + s * C_::STAGE_BYTES;
-                const int kx = (kb0 + i) * BK;
-                if (leader) mbar_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
-                const uint32_t fb = mapa_shared(&full[s], 0);
-                tma_load_3d_pair(st, &tm_ahi, fb, kx, m0, za);
-                tma_load_3d_pair(st + C_::TILE, &tm_alo, fb, kx, m0, za);
-                tma_load_3d_pair(st + 2 * C_::TILE, &tm_bhi, fb, kx, nb0, zb);
-                tma_load_3d_pair(st + 3 * C_::TILE, &tm_blo, fb, kx, nb0, zb);
-                issued = i + 1;
+            uint32_t gs = 0;  // stages issued so far (all units)
+            bool stop = false;
+            for (int u = cluster; u < p.n_units && !stop; u += clusters) {
+                const PairUnit w = pair_unit(p, u, rank, nkb_total);
+                for (int i = 0; i < w.kcount; ++i, ++gs) {
+                    const int s = static_cast<int>(gs % STAGES);
+                    const uint32_t ph = (gs / STAGES) & 1;
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ST_TIMEOUT_EMPTY)) {
+                        stop = true;
+                        break;
+                    }
+                    uint8_t* st = tiles + s * C_::STAGE_BYTES;
+                    const int kx = (w.kb0 + i) * BK;
+                    if (leader) mbar_expect_tx(&full[s], 2 * C_::STAGE_BYTES);
+                    const uint32_t fb = mapa_shared(&full[s], 0);
+                    tma_load_3d_pair(st, &tm_ahi, fb, kx, w.m0, w.za);
+                    tma_load_3d_pair(st + C_::TILE, &tm_alo, fb, kx, w.m0, w.za);
+                    tma_load_3d_pair(st + 2 * C_::TILE, &tm_bhi, fb, kx, w.nb0, w.zb);
+                    tma_load_3d_pair(st + 3 * C_::TILE, &tm_blo, fb, kx, w.nb0, w.zb);
+                }
             }
-            if (*abort_flag && issued > 0) {
+            if (*abort_flag && gs > 0) {
                 if (leader) {
                     // let the copies already issued land before shared memory goes away
-                    for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i) {
+                    for (uint32_t i = (gs > STAGES ? gs - STAGES : 0); i < gs; ++i) {
                         const long long t0 = clock64();
                         while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) && clock64() - t0 < WAIT_BUDGET) {
                         }
@@ -552,33 +578,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
     } else if (warp == 1) {
         if (leader && lane == 0) {
-            for (int i = 0; i < kcount; ++i) {
-                const int s = i % STAGES;
-                const uint32_t ph = (i / STAGES) & 1;
-                const int c = i / p.chunk_kb, within = i - c * p.chunk_kb;
-                const int b = c & 1;
-                if (within == 0) {
-                    if (!mbar_wait_cluster(&tempty[b], ((c >> 1) & 1) ^ 1, abort_flag, p.status, ST_TIMEOUT_TEMPTY))
+            uint32_t gs = 0, gc = 0;  // stages consumed, chunks accumulated (all units)
+            bool stop = false;
+            for (int u = cluster; u < p.n_units && !stop; u += clusters) {
+                const PairUnit w = pair_unit(p, u, rank, nkb_total);
+                for (int i = 0; i < w.kcount; ++i, ++gs) {
+                    const int s = static_cast<int>(gs % STAGES);
+                    const uint32_t ph = (gs / STAGES) & 1;
+                    const int within = i % p.chunk_kb;
+                    const int b = static_cast<int>(gc & 1);
+                    if (within == 0 &&
+                        !mbar_wait_cluster(&tempty[b], ((gc >> 1) & 1) ^ 1, abort_flag, p.status, ST_TIMEOUT_TEMPTY)) {
+                        stop = true;
                         break;
-                }
-                if (!mbar_wait(&full[s], ph, abort_flag, p.status, ST_TIMEOUT_FULL)) break;
-                asm volatile("tcgen05.fence::after_thread_sync;");
-                const uint32_t acc = tmem + static_cast<uint32_t>(b * 256);
-                const uint32_t st = smem_u32(tiles + s * C_::STAGE_BYTES);
-                const uint32_t ahi = st, alo = st + C_::TILE, bhi = st + 2 * C_::TILE, blo = st + 3 * C_::TILE;
+                    }
+                    if (!mbar_wait(&full[s], ph, abort_flag, p.status, ST_TIMEOUT_FULL)) {
+                        stop = true;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    const uint32_t acc = tmem + static_cast<uint32_t>(b * 256);
+                    const uint32_t st = smem_u32(tiles + s * C_::STAGE_BYTES);
+                    const uint32_t ahi = st, alo = st + C_::TILE, bhi = st + 2 * C_::TILE, blo = st + 3 * C_::TILE;
 #pragma unroll
-                for (int k = 0; k < BK / 8; ++k) {
-                    const uint64_t dah = operand_desc<BK>(ahi, k), dal = operand_desc<BK>(alo, k);
-                    const uint64_t dbh = operand_desc<BK>(bhi, k), dbl = operand_desc<BK>(blo, k);
-                    mma_tf32_pair(acc, dah, dbh, kIdescPair, (within | k) != 0);
-                    mma_tf32_pair(acc, dah, dbl, kIdescPair, 1u);
-                    mma_tf32_pair(acc, dal, dbh, kIdescPair, 1u);
-                }
-                mma_commit_pair(mapa_shared(&empty[s], 0));
-                mma_commit_pair(mapa_shared(&empty[s], 1));
-                if (within == p.chunk_kb - 1 || i == kcount - 1) {
-                    mma_commit_pair(mapa_shared(&tfull[b], 0));
-                    mma_commit_pair(mapa_shared(&tfull[b], 1));
+                    for (int k = 0; k < BK / 8; ++k) {
+                        const uint64_t dah = operand_desc<BK>(ahi, k), dal = operand_desc<BK>(alo, k);
+                        const uint64_t dbh = operand_desc<BK>(bhi, k), dbl = operand_desc<BK>(blo, k);
+                        mma_tf32_pair(acc, dah, dbh, kIdescPair, (within | k) != 0);
+                        mma_tf32_pair(acc, dah, dbl, kIdescPair, 1u);
+                        mma_tf32_pair(acc, dal, dbh, kIdescPair, 1u);
+                    }
+                    mma_commit_pair(mapa_shared(&empty[s], 0));
+                    mma_commit_pair(mapa_shared(&empty[s], 1));
+                    if (within == p.chunk_kb - 1 || i == w.kcount - 1) {
+                        mma_commit_pair(mapa_shared(&tfull[b], 0));
+                        mma_commit_pair(mapa_shared(&tfull[b], 1));
+                        ++gc;
+                    }
                 }
             }
         }
@@ -587,35 +623,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         // epilogue warp e (0..7): TMEM lanes 32*(warp%4).., columns 128*(e/4) .. +127
         const int e = warp - 2, q = warp & 3, h = e >> 2;
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-        float acc[128];
-#pragma unroll
-        for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+        const bool vec_ok = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                            (p.c_bstride % 4 == 0);
+        uint32_t ec = 0;  // chunks drained (all units)
         bool ok = true;
-        for (int c = 0; c < nchunks; ++c) {
-            const int b = c & 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (c >> 1) & 1, abort_flag, p.status, ST_TIMEOUT_TFULL));
-            if (!ok) break;
-            asm volatile("tcgen05.fence::after_thread_sync;");
+        for (int u = cluster; u < p.n_units && ok; u += clusters) {
+            const PairUnit w = pair_unit(p, u, rank, nkb_total);
+            const int nchunks = (w.kcount + p.chunk_kb - 1) / p.chunk_kb;
+            float acc[128];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                uint32_t r[32];
-                tmem_ld32(tmem + lane_base + static_cast<uint32_t>(b * 256 + h * 128 + j * 32), r);
+            for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+            for (int c = 0; c < nchunks; ++c, ++ec) {
+                const int b = static_cast<int>(ec & 1);
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait(&tfull[b], (ec >> 1) & 1, abort_flag, p.status, ST_TIMEOUT_TFULL));
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
 #pragma unroll
-                for (int t = 0; t < 32; ++t) acc[j * 32 + t] = __fadd_rn(acc[j * 32 + t], __uint_as_float(r[t]));
+                for (int j = 0; j < 4; ++j) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + lane_base + static_cast<uint32_t>(b * 256 + h * 128 + j * 32), r);
+#pragma unroll
+                    for (int t = 0; t < 32; ++t) acc[j * 32 + t] = __fadd_rn(acc[j * 32 + t], __uint_as_float(r[t]));
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;");
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(&tempty[b], 0));
             }
-            asm volatile("tcgen05.fence::before_thread_sync;");
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa_shared(&tempty[b], 0));
-        }
-        if (ok) {
-            const int row = m0 + q * 32 + lane;
-            float* crow = p.C + static_cast<int64_t>(zb_all) * p.c_bstride + static_cast<int64_t>(row) * p.ldc;
-            const bool vec_ok = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
-                                (p.c_bstride % 4 == 0);
+            if (!ok) break;
+            const int row = w.m0 + q * 32 + lane;
+            float* crow = p.C + static_cast<int64_t>(w.zb_all) * p.c_bstride + static_cast<int64_t>(row) * p.ldc;
             if (row < p.M) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const int col0 = n0 + h * 128 + j * 32;
+                    const int col0 = w.n0 + h * 128 + j * 32;
                     if (col0 < p.N) {
                         float v[32];
 #pragma unroll
@@ -873,17 +914,36 @@ int launch_main(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
     return static_cast<int>(cudaGetLastError());
 }
 
+// Persistent launch: one cluster per co-resident SM pair (at most one per work unit).
 template <int BK>
 int launch_pair(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
-                const TcParams& p, dim3 grid, cudaStream_t st) {
+                const TcParams& p, cudaStream_t st) {
     static std::once_flag once;
     static cudaError_t err = cudaSuccess;
+    static int max_clusters = 0;
     std::call_once(once, [] {
         err = cudaFuncSetAttribute(gemm_tc_pair_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    PairCfg<BK>::SMEM_BYTES);
+        if (err != cudaSuccess) return;
+        int dev = 0, sms = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(sms > 1 ? sms : 2), 1, 1);
+        cfg.blockDim = dim3(THREADS, 1, 1);
+        cfg.dynamicSmemBytes = PairCfg<BK>::SMEM_BYTES;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_pair_kernel<BK>, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = sms / 2 > 0 ? sms / 2 : 1;
+        }
+        max_clusters = n;
     });
     if (err != cudaSuccess) return static_cast<int>(err);
-    gemm_tc_pair_kernel<BK><<<grid, THREADS, PairCfg<BK>::SMEM_BYTES, st>>>(ahi, alo, bhi, blo, p);
+    const int clusters = p.n_units < max_clusters ? p.n_units : max_clusters;
+    if (clusters <= 0) return 0;
+    gemm_tc_pair_kernel<BK><<<dim3(static_cast<unsigned>(2 * clusters)), THREADS, PairCfg<BK>::SMEM_BYTES, st>>>(
+        ahi, alo, bhi, blo, p);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -998,9 +1058,10 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
         p.epilogue = d.epilogue;
     }
     if (d.pair) {
-        dim3 grid(static_cast<unsigned>(2 * ((d.N + 255) / 256)), static_cast<unsigned>((d.M + 255) / 256),
-                  static_cast<unsigned>(d.batch * d.ksplit));
-        rc = launch_pair<32>(m_ahi, m_alo, m_bhi, m_blo, p, grid, st);
+        p.tiles_m = static_cast<int>((d.M + 255) / 256);
+        p.tiles_n = static_cast<int>((d.N + 255) / 256);
+        p.n_units = static_cast<int>(p.tiles_m * p.tiles_n * d.batch * d.ksplit);
+        rc = launch_pair<32>(m_ahi, m_alo, m_bhi, m_blo, p, st);
     } else {
         dim3 grid(static_cast<unsigned>((d.N + BN - 1) / BN), static_cast<unsigned>((d.M + BM - 1) / BM),
                   static_cast<unsigned>(d.batch * d.ksplit));
