@@ -306,3 +306,34 @@ def test_bounded_wait_selftest_rejects_unbounded_budgets():
     status = ctypes.c_int32(0)
     with pytest.raises(ValueError):
         _lib.check(_lib.lib.tt_selftest_bounded_wait(10**12, ctypes.byref(status)))
+
+
+def test_activations_fold_into_gemm_epilogues(cache_dir):
+    """A ReLU or tanh whose only input is a matmul runs in that GEMM's epilogue; the
+    ReLU's backward mask reads the ReLU output (the same mask), so the forward matmul
+    keeps a single reader and no separate activation pass remains."""
+    g = tt.Graph()
+    x, w1, w2 = g.input([256, 192]), g.input([192, 320]), g.input([320, 64])
+    loss = tt.mean(tt.tanh(tt.relu(x @ w1) @ w2))
+    plan = tt.compile_gradients(g, loss, [w1, w2], cache_dir=cache_dir, flags=HOST).execution_plan()
+    gemms = [line for line in plan.splitlines() if "] gemm/" in line]
+    assert sum("+relu]" in line for line in gemms) == 1 and sum("+tanh]" in line for line in gemms) == 1, plan
+    regions = [line for line in plan.splitlines() if "fused[" in line]
+    assert not any("relu" in line or "tanh" in line for line in regions), plan
+    # TT_FLAG_NO_GEMM_FUSION keeps the epilogues plain
+    plain = tt.compile_gradients(g, loss, [w1, w2], cache_dir=cache_dir,
+                                 flags=HOST | tt.FLAG_NO_GEMM_FUSION).execution_plan()
+    assert "+relu]" not in plain and "+tanh]" not in plain
+
+
+def test_matmul_with_another_reader_keeps_its_activation_apart(cache_dir):
+    g = tt.Graph()
+    a, b = g.input([256, 128]), g.input([128, 256])
+    m = a @ b
+    plan = _host_compile(g, [tt.relu(m), m * 2.0], cache_dir).execution_plan()
+    assert "+relu]" not in plan and "relu" in plan
+    # the activation as a graph output: the GEMM writes that output directly
+    g2 = tt.Graph()
+    a2, b2 = g2.input([256, 128]), g2.input([128, 256])
+    plan2 = _host_compile(g2, [tt.tanh(a2 @ b2)], cache_dir).execution_plan()
+    assert "+tanh] -> output:0" in plan2 and "Kernel Launches (1)" in plan2, plan2

@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const float* __restrict_
             const int64_t gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
             if (gn < N) {
                 float v = acc[i][j];
-                if (EPI == EP_RELU) v = v > 0.0f ? v : 0.0f;
+                v = gemm_epilogue(v, EPI);
                 C[gm * N + gn] = v;
             }
         }
@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(128 * G) gemm_skinny_kernel(
             const int64_t q = g * 8 + j;
             if (q < Q) {
                 float v = __fadd_rn(tot[j], acc[j]);
-                if (epilogue == EP_RELU) v = v > 0.0f ? v : 0.0f;
+                v = gemm_epilogue(v, epilogue);
                 C[r * c_sr + q * c_sq] = v;
             }
         }
@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(128) gemm_skinny_async_kernel(
         for (int j = 0; j < NQ; ++j) {
             if (j < Q) {
                 float v = __fadd_rn(tot[j], acc[j]);
-                if (epilogue == EP_RELU) v = v > 0.0f ? v : 0.0f;
+                v = gemm_epilogue(v, epilogue);
                 C[r * c_sr + j * c_sq] = v;
             }
         }
@@ -496,9 +496,9 @@ __global__ void __launch_bounds__(256) gemm_smallk_kernel(const float* __restric
                     v[3] = fmaf(av[j], b.w, v[3]);
                 }
             }
-            if (EPI == EP_RELU) {
+            if (EPI != EP_NONE) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
+                for (int j = 0; j < 4; ++j) v[j] = gemm_epilogue(v[j], EPI);
             }
             if (m >= M) continue;
             float* crow = C + m * N;
@@ -534,6 +534,9 @@ void launch_smallk_t(const GemmDesc& d, const float* A, const float* B, float* C
     const int K = static_cast<int>(d.K);
     if (d.epilogue == EP_RELU)
         gemm_smallk_kernel<KP, EP_RELU><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, K, d.a_sm, d.a_sk, d.a_sb, d.b_sk,
+                                                              d.b_sn, d.b_sb, d.c_sb, vec);
+    else if (d.epilogue == EP_TANH)
+        gemm_smallk_kernel<KP, EP_TANH><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, K, d.a_sm, d.a_sk, d.a_sb, d.b_sk,
                                                               d.b_sn, d.b_sb, d.c_sb, vec);
     else
         gemm_smallk_kernel<KP, EP_NONE><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, K, d.a_sm, d.a_sk, d.a_sb, d.b_sk,
@@ -709,6 +712,9 @@ int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, voi
               static_cast<unsigned>(d.batch));
     if (d.epilogue == EP_RELU)
         gemm_simt_kernel<EP_RELU><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, d.K, d.a_sm, d.a_sk, d.a_sb, d.b_sk, d.b_sn,
+                                                        d.b_sb, d.c_sb);
+    else if (d.epilogue == EP_TANH)
+        gemm_simt_kernel<EP_TANH><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, d.K, d.a_sm, d.a_sk, d.a_sb, d.b_sk, d.b_sn,
                                                         d.b_sb, d.c_sb);
     else
         gemm_simt_kernel<EP_NONE><<<grid, 256, 0, st>>>(A, B, C, d.M, d.N, d.K, d.a_sm, d.a_sk, d.a_sb, d.b_sk, d.b_sn,

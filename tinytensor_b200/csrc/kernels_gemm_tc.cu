@@ -333,8 +333,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         float v[32];
 #pragma unroll
                         for (int t = 0; t < 32; ++t) {
-                            v[t] = acc[j * 32 + t];
-                            if (p.epilogue == EP_RELU) v[t] = v[t] > 0.0f ? v[t] : 0.0f;
+                            v[t] = gemm_epilogue(acc[j * 32 + t], p.epilogue);
                         }
                         if (vec_ok && col0 + 32 <= p.N) {
 #pragma unroll
@@ -661,8 +660,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                         float v[32];
 #pragma unroll
                         for (int t = 0; t < 32; ++t) {
-                            v[t] = acc[j * 32 + t];
-                            if (p.epilogue == EP_RELU) v[t] = v[t] > 0.0f ? v[t] : 0.0f;
+                            v[t] = gemm_epilogue(acc[j * 32 + t], p.epilogue);
                         }
                         if (vec_ok && col0 + 32 <= p.N) {
 #pragma unroll
@@ -705,12 +703,10 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
                 v.z = __fadd_rn(v.z, x.z);
                 v.w = __fadd_rn(v.w, x.w);
             }
-            if (epilogue == EP_RELU) {
-                v.x = v.x > 0.0f ? v.x : 0.0f;
-                v.y = v.y > 0.0f ? v.y : 0.0f;
-                v.z = v.z > 0.0f ? v.z : 0.0f;
-                v.w = v.w > 0.0f ? v.w : 0.0f;
-            }
+            v.x = gemm_epilogue(v.x, epilogue);
+            v.y = gemm_epilogue(v.y, epilogue);
+            v.z = gemm_epilogue(v.z, epilogue);
+            v.w = gemm_epilogue(v.w, epilogue);
             *reinterpret_cast<float4*>(C + b * c_bstride + i) = v;
         }
         return;
@@ -718,8 +714,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < per; i += stride) {
         float v = 0.0f;
         for (int s = 0; s < ksplit; ++s) v = __fadd_rn(v, __ldg(P + (b * ksplit + s) * per + i));
-        if (epilogue == EP_RELU) v = v > 0.0f ? v : 0.0f;
-        C[b * c_bstride + i] = v;
+        C[b * c_bstride + i] = gemm_epilogue(v, epilogue);
     }
 }
 

@@ -42,14 +42,22 @@ int64_t reduce_prepare(ReduceDesc& d);
 int launch_reduce(const ReduceDesc& d, const float* in, float* out, void* scratch, void* stream);
 
 // ---- GEMM (kernels_gemm.cu) ----
-enum Epilogue { EP_NONE = 0, EP_RELU = 1 };
+enum Epilogue { EP_NONE = 0, EP_RELU = 1, EP_TANH = 2 };
+#ifdef __CUDACC__
+// The activation a GEMM applies to each output element in its epilogue: the same
+// expressions as the generated elementwise kernels (ReLU as x > 0 ? x : 0, so NaN and
+// -0 give +0; tanh as tanhf).
+__device__ __forceinline__ float gemm_epilogue(float v, int ep) {
+    return ep == EP_RELU ? (v > 0.0f ? v : 0.0f) : ep == EP_TANH ? tanhf(v) : v;
+}
+#endif
 struct GemmDesc {
     int64_t M = 0, N = 0, K = 0, batch = 1;
     int64_t a_sm = 0, a_sk = 0, a_sb = 0;  // A[b][m][k] element strides
     int64_t b_sk = 0, b_sn = 0, b_sb = 0;  // B[b][k][n]
     int64_t c_sb = 0;                      // C[b][m][n] row stride N
     int64_t a_off = 0, b_off = 0;          // element offsets of the operand views
-    int epilogue = EP_NONE;
+    int epilogue = EP_NONE;                // activation applied to C (a ReLU / tanh folded into the GEMM)
     int algo = 0;                          // chosen by plan_gemm
     int ksplit = 1;                        // tensor-core kernel: K split across CTAs
     int chunk_kb = 8;                      // tensor-core kernel: K blocks per TMEM chunk

@@ -61,6 +61,44 @@ Access broadcast_access(const Storage& s, int node, const Shape& from, const Sha
     return a;
 }
 
+// GEMM epilogues.  (a) The ReLU derivative mask step(x) equals step(relu(x)) bit for
+// bit (relu maps NaN and -0 to +0, and step maps +0, -0 and NaN alike to 0), so a mask
+// reads the ReLU's output when the graph has one; the matmul before the ReLU then has
+// no other reader.  (b) A matmul whose only reader is a ReLU or tanh (the matmul not a
+// graph output) applies the activation in its own epilogue and stores the activated
+// value; the activation node becomes a view of the matmul's storage (or, when it is a
+// graph output, the matmul writes that output).  This removes one HBM pass over the
+// activation (read + write) per folded node.
+void fold_gemm_epilogues(Graph& g, const std::vector<int>& out_pos) {
+    const size_t n = g.nodes.size();
+    std::vector<int> relu_of(n, -1);
+    for (size_t i = 0; i < n; ++i)
+        if (g.nodes[i].op == TT_OP_RELU) {
+            const size_t x = static_cast<size_t>(g.nodes[i].in[0]);
+            if (relu_of[x] < 0) relu_of[x] = static_cast<int>(i);
+        }
+    for (size_t i = 0; i < n; ++i) {
+        Node& s = g.nodes[i];
+        if (s.op != TT_OP_STEP) continue;
+        const int r = relu_of[static_cast<size_t>(s.in[0])];
+        if (r >= 0 && r < static_cast<int>(i)) s.in[0] = r;  // keeps the node order topological
+    }
+    std::vector<int> readers(n, 0), reader(n, -1);
+    for (size_t i = 0; i < n; ++i)
+        for (int q : g.nodes[i].in) {
+            ++readers[static_cast<size_t>(q)];
+            reader[static_cast<size_t>(q)] = static_cast<int>(i);
+        }
+    for (size_t m = 0; m < n; ++m) {
+        Node& mm = g.nodes[m];
+        if (mm.op != TT_OP_MATMUL || out_pos[m] >= 0 || readers[m] != 1) continue;
+        Node& a = g.nodes[static_cast<size_t>(reader[m])];
+        if ((a.op != TT_OP_RELU && a.op != TT_OP_TANH) || a.shape != mm.shape) continue;
+        mm.epilogue = a.op == TT_OP_RELU ? EP_RELU : EP_TANH;
+        a.fused_into = static_cast<int>(m);
+    }
+}
+
 }  // namespace
 
 Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
@@ -71,6 +109,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
 
     std::vector<int> out_pos(N0, -1);
     for (size_t k = 0; k < g.outputs.size(); ++k) out_pos[static_cast<size_t>(g.outputs[k])] = static_cast<int>(k);
+    if (opt.gemm_epilogue) fold_gemm_epilogues(g, out_pos);
     std::vector<std::vector<int>> users(N0);
     for (size_t i = 0; i < N0; ++i)
         for (int q : g.nodes[i].in) users[static_cast<size_t>(q)].push_back(static_cast<int>(i));
@@ -87,7 +126,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         }
         if (n.dtype != TT_FLOAT32) fail(TT_ERR_COMPILE, "The CUDA backend computes in float32 only (node %" +
                                                             std::to_string(n.id) + " is float64)");
-        if (is_elementwise(n.op)) {
+        if (is_elementwise(n.op) && n.fused_into < 0) {
             int R = -1;
             if (opt.fuse) {
                 for (int q : n.in) {
@@ -131,7 +170,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
             const Node& n = g.nodes[i];
             if (p.region_of[i] >= 0) unit_of[i] = p.region_of[i];
             else if (n.op == TT_OP_MATMUL || is_reduce(n.op)) unit_of[i] = nu++;
-            else if (is_view(n.op)) unit_of[i] = unit_of[static_cast<size_t>(n.in[0])];
+            else if (is_view(n.op) || n.fused_into >= 0) unit_of[i] = unit_of[static_cast<size_t>(n.in[0])];
         }
         std::vector<int> alias(static_cast<size_t>(nu));
         for (int u = 0; u < nu; ++u) alias[static_cast<size_t>(u)] = u;
@@ -143,7 +182,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
             changed = false;
             std::vector<std::set<int>> succ(static_cast<size_t>(nu));
             for (size_t i = 0; i < N0; ++i) {
-                if (unit_of[i] < 0 || is_view(g.nodes[i].op)) continue;
+                if (unit_of[i] < 0 || is_view(g.nodes[i].op) || g.nodes[i].fused_into >= 0) continue;
                 int ui = find(unit_of[i]);
                 for (int q : g.nodes[i].in) {
                     int uq = unit_of[static_cast<size_t>(q)];
@@ -201,7 +240,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
     // ---- 2. storage ----
     std::vector<bool> stored(N0, false);
     for (size_t i = 0; i < N0; ++i) {
-        if (!is_elementwise(g.nodes[i].op)) continue;
+        if (!is_elementwise(g.nodes[i].op) || g.nodes[i].fused_into >= 0) continue;
         bool s = out_pos[i] >= 0;
         for (int u : users[i]) s |= p.region_of[static_cast<size_t>(u)] != p.region_of[i];
         stored[i] = s;
@@ -227,6 +266,10 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
     };
     for (size_t i = 0; i < N0; ++i) {
         const Node& n = g.nodes[i];
+        if (n.fused_into >= 0) {  // computed by the matmul's epilogue: a view of its storage
+            p.st[i] = p.st[static_cast<size_t>(n.fused_into)];
+            continue;
+        }
         switch (n.op) {
             case TT_OP_INPUT:
                 p.st[i] = make_root(i);
@@ -425,12 +468,13 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         int n = g.outputs[k];
         const Node& nd = g.nodes[static_cast<size_t>(n)];
         const Storage& s = p.st[static_cast<size_t>(n)];
-        bool own = s.kind == SK_BUF && s.root == n && nd.op != TT_OP_INPUT && nd.op != TT_OP_CONSTANT;
+        const bool folded = nd.fused_into >= 0 && s.kind == SK_BUF && s.root == nd.fused_into;  // GEMM epilogue
+        bool own = (s.kind == SK_BUF && s.root == n && nd.op != TT_OP_INPUT && nd.op != TT_OP_CONSTANT) || folded;
         if (own) {
             BufRef r;
             r.kind = BK_OUTPUT;
             r.index = static_cast<int>(k);
-            p.root_ref[static_cast<size_t>(n)] = r;
+            p.root_ref[static_cast<size_t>(s.root)] = r;
         } else {
             Region r;
             r.shape = nd.shape;
@@ -656,6 +700,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
             d.a_sb = bstride(sa, A.shape, ra);
             d.b_sb = bstride(sb, B.shape, rb);
             d.c_sb = d.M * d.N;
+            d.epilogue = n.epilogue;
             if (d.M == 1) d.a_sm = d.a_sk == 1 ? d.K : 1;
             plan_gemm(d);
             L.scratch_bytes = gemm_scratch_bytes(d);
@@ -663,7 +708,9 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
             lb << "gemm/" << gemm_algo_name(d.algo) << "[" << d.M << "x" << d.N << "x" << d.K;
             if (d.batch > 1) lb << " b" << d.batch;
             if (d.ksplit > 1) lb << " splitk" << d.ksplit;
-            lb << (d.a_sk == 1 ? " A:K" : " A:M") << (d.b_sn == 1 ? " B:N" : " B:K") << "]";
+            lb << (d.a_sk == 1 ? " A:K" : " A:M") << (d.b_sn == 1 ? " B:N" : " B:K");
+            if (d.epilogue != EP_NONE) lb << (d.epilogue == EP_RELU ? " +relu" : " +tanh");
+            lb << "]";
             L.label = lb.str();
         }
         p.launches.push_back(L);

@@ -33,6 +33,10 @@ struct Node {
     bool keepdims = false;
     std::vector<float> cdata;  // Constant payload (float32)
     std::string name, expr;
+    // Set by the scheduler only: a matmul's epilogue activation (program.hpp Epilogue),
+    // and on that activation node the index of the matmul that computes it.
+    int epilogue = 0;
+    int fused_into = -1;
 };
 
 struct Graph {
