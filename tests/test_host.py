@@ -337,3 +337,37 @@ def test_matmul_with_another_reader_keeps_its_activation_apart(cache_dir):
     a2, b2 = g2.input([256, 128]), g2.input([128, 256])
     plan2 = _host_compile(g2, [tt.tanh(a2 @ b2)], cache_dir).execution_plan()
     assert "+tanh] -> output:0" in plan2 and "Kernel Launches (1)" in plan2, plan2
+
+
+def test_dz_regions_write_the_gemm_operand_copies(cache_dir):
+    """In the MLP backward pass the dZ regions write the hi/lo copies their tensor-core
+    GEMMs read (dZ2 in both layouts for dW2 = H1^T dZ2 and dH1 = dZ2 W2^T, dZ1
+    transposed for dW1 = X^T dZ1) and no fp32 dZ; those GEMMs run no pre-pass for that
+    operand, and the copies' buffer stays apart from every buffer of the launches it
+    outlives."""
+    g = tt.Graph()
+    x, t = g.input([4096, 1024]), g.input([4096, 10])
+    w1, w2, w3 = g.input([1024, 4096]), g.input([4096, 4096]), g.input([4096, 10])
+    d = tt.tanh(tt.relu(x @ w1) @ w2) @ w3 - t
+    loss = tt.mean(d * d)
+    plan = tt.compile_gradients(g, loss, [w1, w2, w3], cache_dir=cache_dir, flags=HOST).execution_plan()
+    lines = [line.strip() for line in plan.splitlines() if line.strip().startswith("[")]
+    producers = [i for i, line in enumerate(lines) if "(writes hi/lo of" in line]
+    assert len(producers) == 2, plan
+    both, tr = lines[producers[0]], lines[producers[1]]
+    assert "(writes hi/lo of X and X^T, not X)" in both and "(writes hi/lo of X^T, not X)" in tr, plan
+    readers = [line for line in lines if "hi/lo from [" in line]
+    assert len(readers) == 3 and all("tcgen05" in line for line in readers), plan
+    for p in producers:
+        m = re.search(r"copies=(\d+)@(\d+)", lines[p])
+        size, off = int(m.group(1)), int(m.group(2))
+        last = max(i for i, line in enumerate(lines) if f"hi/lo from [{p}])" in line)
+        for line in lines[p + 1: last + 1]:
+            for sz, o in re.findall(r"scratch=(\d+)@(\d+)", line):
+                assert int(o) + int(sz) <= off or off + size <= int(o), line
+            for o in re.findall(r"(?:-> |copies=\d+@)arena:(\d+)", line):
+                assert not (off <= int(o) < off + size), line
+    # TT_FLAG_NO_GEMM_FUSION: plain regions, every GEMM splits its own operands
+    plain = tt.compile_gradients(g, loss, [w1, w2, w3], cache_dir=cache_dir,
+                                 flags=HOST | tt.FLAG_NO_GEMM_FUSION).execution_plan()
+    assert "hi/lo" not in plain

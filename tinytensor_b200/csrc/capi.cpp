@@ -347,6 +347,14 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
                     vals.push_back(a.imm ? nullptr : resolve(pl.root_ref[static_cast<size_t>(a.node)]));
                 }
                 for (const BufRef& b : r.store_ref) vals.push_back(resolve(b));
+                if (r.copy_store >= 0) {  // hi/lo operand copies: [R][C] hi, lo, then [C][R] hi, lo
+                    char* base = resolve(L.split_ref);
+                    for (int layout = 0; layout < 2; ++layout)
+                        for (int lo = 0; lo < 2; ++lo)
+                            vals.push_back((layout == 0 ? r.copy_rows : r.copy_t)
+                                               ? base + split_copies_offset(r.copy_R, r.copy_C, r.copy_rows, layout, lo)
+                                               : nullptr);
+                }
                 std::vector<void*> args;
                 for (void*& v : vals) args.push_back(&v);
                 CUresult cr = driver().launchKernel(p->region_fn[static_cast<size_t>(L.region)],
@@ -358,9 +366,20 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
             rc = launch_reduce(L.rd, reinterpret_cast<const float*>(resolve(L.in_ref)),
                                reinterpret_cast<float*>(resolve(L.out_ref)), resolve(L.scratch_ref), st);
         } else {
+            // operands whose hi/lo copies the producing region wrote
+            GemmSplitIO io;
+            auto copies = [&](int src, int layout, const float*& hi, const float*& lo) {
+                const Launch& P = pl.launches[static_cast<size_t>(src)];
+                const Region& r = pl.regions[static_cast<size_t>(P.region)];
+                char* base = resolve(P.split_ref);
+                hi = reinterpret_cast<const float*>(base + split_copies_offset(r.copy_R, r.copy_C, r.copy_rows, layout, 0));
+                lo = reinterpret_cast<const float*>(base + split_copies_offset(r.copy_R, r.copy_C, r.copy_rows, layout, 1));
+            };
+            if (L.gd.a_presplit) copies(L.a_split_src, L.a_split_layout, io.a_hi, io.a_lo);
+            if (L.gd.b_presplit) copies(L.b_split_src, L.b_split_layout, io.b_hi, io.b_lo);
             rc = launch_gemm(L.gd, reinterpret_cast<const float*>(resolve(L.in_ref)),
                              reinterpret_cast<const float*>(resolve(L.in_ref2)),
-                             reinterpret_cast<float*>(resolve(L.out_ref)), resolve(L.scratch_ref), status, st);
+                             reinterpret_cast<float*>(resolve(L.out_ref)), resolve(L.scratch_ref), status, st, &io);
         }
         if (rc) fail(TT_ERR_RUNTIME, L.label + ": " + cudaGetErrorString(static_cast<cudaError_t>(rc)));
         g_launches += static_cast<uint64_t>(launches_of(pl, L));

@@ -31,9 +31,151 @@ struct Dim {
     std::vector<int64_t> st;  // per access: ext accesses then stores
 };
 
+// The expression of one region node, operands x (and y).
+std::string node_expr(const Node& nd, const std::string& x, const std::string& y) {
+    std::ostringstream ss;
+    switch (nd.op) {
+        case TT_OP_ADD: ss << x << " + " << y; break;
+        case TT_OP_SUB: ss << x << " - " << y; break;
+        case TT_OP_MUL: ss << x << " * " << y; break;
+        case TT_OP_DIV: ss << x << " / " << y; break;
+        case TT_OP_RELU: ss << "(" << x << " > 0.0f) ? " << x << " : 0.0f"; break;
+        case TT_OP_STEP: ss << "(" << x << " > 0.0f) ? 1.0f : 0.0f"; break;
+        case TT_OP_NEG: ss << "-" << x; break;
+        case TT_OP_EXP: ss << "tt_exp(" << x << ")"; break;
+        case TT_OP_TANH: ss << "tt_tanh(" << x << ")"; break;
+        case TT_OP_SIGMOID: ss << "tt_sigmoid(" << x << ")"; break;
+        default: fail(TT_ERR_COMPILE, "internal: non-elementwise op in region");
+    }
+    return ss.str();
+}
+
+int64_t round4c(int64_t x) { return (x + 3) / 4 * 4; }
+
 }  // namespace
 
+// A region that also writes hi/lo operand copies of its stored [R][C] matrix X (for
+// tensor-core GEMMs that read X without a pre-pass of their own).  A CTA computes one
+// 32-row x 128-column tile: each warp takes rows w, w+8, w+16, w+24 with a float4 of
+// columns per lane (coalesced loads, fp32 stores and row-layout copies), parks the
+// tile in shared memory (row pitch 129 floats: conflict-free column reads), then each
+// warp writes 16 columns of the transposed copies with lane = row (128-B runs).  Tiles
+// are numbered rows first, so the CTAs resident together write neighbouring runs of
+// each transposed row; one CTA per tile (the hardware balances the SMs).
+static void emit_region_tiled(std::ostringstream& ss, const Plan& p, Region& r) {
+    const Graph& g = p.g;
+    const size_t next = r.ext.size(), nsto = r.store_ref.size();
+    const int64_t R = r.copy_R, C = r.copy_C, Cp = round4c(C), Rp = round4c(R);
+    const int64_t tiles_r = (R + 31) / 32, tiles = tiles_r * ((C + 127) / 128);
+    r.vec = 4;
+    r.unroll = 1;
+    r.grid = tiles;
+    int64_t maxoff = std::max(R * Cp, C * Rp);
+    for (size_t e = 0; e < next; ++e) {
+        const Access& a = r.ext_access[e];
+        if (!a.imm) maxoff = std::max(maxoff, a.offset + (R - 1) * a.strides[0] + (C - 1) * a.strides[1] + 1);
+    }
+    const char* it = maxoff < (1LL << 31) - 1024 ? "int" : "long long";
+    const size_t cs = static_cast<size_t>(r.copy_store);
+    ss << "// region " << r.kernel << ": fused over " << shape_str(r.shape) << ", tiled, hi/lo copies of store " << cs
+       << (r.copy_rows ? " [R][C]" : "") << (r.copy_t ? " [C][R]" : "") << (r.drop_f32 ? ", its fp32 not stored" : "")
+       << "\n";
+    ss << "extern \"C\" __global__ void __launch_bounds__(256) " << r.kernel << "(";
+    for (size_t e = 0; e < next; ++e) ss << (e ? ", " : "") << "const float* __restrict__ x" << e;
+    for (size_t k = 0; k < nsto; ++k) ss << (next + k ? ", " : "") << "float* __restrict__ y" << k;
+    ss << ", float* __restrict__ ch, float* __restrict__ cl, float* __restrict__ th, float* __restrict__ tl) {\n";
+    ss << "  typedef " << it << " I;\n";
+    ss << "  __shared__ float tile[32][129];\n";
+    ss << "  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;\n";
+    ss << "  {\n    const I t = blockIdx.x;\n";
+    ss << "    const I r0 = (t % " << tiles_r << ") * 32, c0 = (t / " << tiles_r << ") * 128;\n";
+    ss << "    const I c = c0 + 4 * lane;\n";
+    ss << "#pragma unroll\n    for (int i = 0; i < 4; ++i) {\n";
+    ss << "      const I rr = r0 + w + 8 * i;\n";
+    ss << "      const bool rin = rr < (I)" << R << ", full = rin && c + 3 < (I)" << C << ";\n";
+    // loads: a<e>[l] for the four columns c..c+3 of row rr (0 outside X)
+    for (size_t e = 0; e < next; ++e) {
+        const Access& a = r.ext_access[e];
+        if (a.imm) {
+            ss << "      const float a" << e << " = " << flit(a.value) << ";\n";
+            continue;
+        }
+        const int64_t sr = a.strides[0], sc = a.strides[1];
+        std::ostringstream base;
+        base << a.offset << " + rr * (I)" << sr;
+        if (sc == 0) {
+            ss << "      const float a" << e << " = rin ? __ldg(x" << e << " + (" << base.str() << ")) : 0.0f;\n";
+        } else if (sc == 1 && sr % 4 == 0 && a.offset % 4 == 0 && C % 4 == 0) {
+            ss << "      float a" << e << "[4] = {0.0f, 0.0f, 0.0f, 0.0f};\n";
+            ss << "      if (full) { const float4 q = __ldg(reinterpret_cast<const float4*>(x" << e << " + (" << base.str()
+               << " + c))); a" << e << "[0] = q.x; a" << e << "[1] = q.y; a" << e << "[2] = q.z; a" << e << "[3] = q.w; }\n";
+        } else {
+            ss << "      float a" << e << "[4];\n";
+            ss << "#pragma unroll\n      for (int l = 0; l < 4; ++l) a" << e << "[l] = (rin && c + l < (I)" << C
+               << ") ? __ldg(x" << e << " + (" << base.str() << " + (c + l) * (I)" << sc << ")) : 0.0f;\n";
+        }
+    }
+    auto ref = [&](int node) -> std::string {
+        auto itx = std::find(r.ext.begin(), r.ext.end(), node);
+        if (itx != r.ext.end()) {
+            const size_t e = static_cast<size_t>(itx - r.ext.begin());
+            const Access& a = r.ext_access[e];
+            const bool lanes = !a.imm && a.strides[1] != 0;
+            return "a" + std::to_string(e) + (lanes ? "[l]" : "");
+        }
+        return "v" + std::to_string(node);
+    };
+    for (size_t k = 0; k < nsto; ++k) ss << "      float o" << k << "[4];\n";
+    ss << "#pragma unroll\n      for (int l = 0; l < 4; ++l) {\n";
+    for (int i : r.nodes) {
+        const Node& nd = g.nodes[static_cast<size_t>(i)];
+        ss << "        const float v" << i << " = "
+           << node_expr(nd, ref(nd.in[0]), nd.in.size() > 1 ? ref(nd.in[1]) : "") << ";\n";
+    }
+    for (size_t k = 0; k < nsto; ++k) ss << "        o" << k << "[l] = v" << r.stores[k] << ";\n";
+    ss << "      }\n";
+    // fp32 stores of [R][C] matrices (row stride C)
+    for (size_t k = 0; k < nsto; ++k) {
+        if (k == cs && r.drop_f32) continue;
+        if (C % 4 == 0)
+            ss << "      if (full) *reinterpret_cast<float4*>(y" << k << " + rr * (I)" << C << " + c) = make_float4(o" << k
+               << "[0], o" << k << "[1], o" << k << "[2], o" << k << "[3]);\n      else";
+        ss << "      if (rin) { for (int l = 0; l < 4; ++l) if (c + l < (I)" << C << ") y" << k << "[rr * (I)" << C
+           << " + c + l] = o" << k << "[l]; }\n";
+    }
+    if (r.copy_rows) {  // copies in X's layout, row pitch round4(C)
+        ss << "      if (rin) {\n        float4 h, q;\n";
+        ss << "        tt_split(o" << cs << "[0], h.x, q.x); tt_split(o" << cs << "[1], h.y, q.y);\n";
+        ss << "        tt_split(o" << cs << "[2], h.z, q.z); tt_split(o" << cs << "[3], h.w, q.w);\n";
+        ss << "        if (c + 3 < (I)" << C << ") { *reinterpret_cast<float4*>(ch + rr * (I)" << Cp
+           << " + c) = h; *reinterpret_cast<float4*>(cl + rr * (I)" << Cp << " + c) = q; }\n";
+        ss << "        else { const float hv[4] = {h.x, h.y, h.z, h.w}, lv[4] = {q.x, q.y, q.z, q.w};\n";
+        ss << "          for (int l = 0; l < 4; ++l) if (c + l < (I)" << C << ") { ch[rr * (I)" << Cp
+           << " + c + l] = hv[l]; cl[rr * (I)" << Cp << " + c + l] = lv[l]; } }\n";
+        ss << "      }\n";
+    }
+    if (r.copy_t) {
+        ss << "      tile[w + 8 * i][4 * lane] = o" << cs << "[0]; tile[w + 8 * i][4 * lane + 1] = o" << cs << "[1];\n";
+        ss << "      tile[w + 8 * i][4 * lane + 2] = o" << cs << "[2]; tile[w + 8 * i][4 * lane + 3] = o" << cs << "[3];\n";
+    }
+    ss << "    }\n";
+    if (r.copy_t) {  // transposed copies [C][round4(R)]: lane = row, one 128-B run per column
+        ss << "    __syncthreads();\n";
+        ss << "#pragma unroll 4\n    for (int j = 0; j < 16; ++j) {\n";
+        ss << "      const I cc = c0 + w * 16 + j, rr = r0 + lane;\n";
+        ss << "      if (cc < (I)" << C << " && rr < (I)" << R << ") {\n";
+        ss << "        float h, q;\n        tt_split(tile[lane][w * 16 + j], h, q);\n";
+        ss << "        th[cc * (I)" << Rp << " + rr] = h;\n        tl[cc * (I)" << Rp << " + rr] = q;\n      }\n";
+        ss << "    }\n    __syncthreads();\n";
+    }
+    ss << "  }\n}\n\n";
+}
+
 static void emit_region(std::ostringstream& ss, const Plan& p, Region& r) {
+    if (r.copy_store >= 0) {
+        emit_region_tiled(ss, p, r);
+        return;
+    }
     const Graph& g = p.g;
     const size_t next = r.ext.size();
     const size_t nsto = r.store_ref.size();
@@ -163,23 +305,7 @@ static void emit_region(std::ostringstream& ss, const Plan& p, Region& r) {
         const Node& nd = g.nodes[static_cast<size_t>(i)];
         std::string x = ref(nd.in[0]);
         std::string y = nd.in.size() > 1 ? ref(nd.in[1]) : "";
-        ss << "      const float v" << i << " = ";
-        switch (nd.op) {
-            case TT_OP_ADD: ss << x << " + " << y; break;
-            case TT_OP_SUB: ss << x << " - " << y; break;
-            case TT_OP_MUL: ss << x << " * " << y; break;
-            case TT_OP_DIV: ss << x << " / " << y; break;
-            case TT_OP_RELU: ss << "(" << x << " > 0.0f) ? " << x << " : 0.0f"; break;
-            case TT_OP_STEP: ss << "(" << x << " > 0.0f) ? 1.0f : 0.0f"; break;
-            case TT_OP_NEG: ss << "-" << x; break;
-            case TT_OP_EXP: ss << "tt_exp(" << x << ")"; break;
-            case TT_OP_TANH: ss << "tt_tanh(" << x << ")"; break;
-            case TT_OP_SIGMOID:
-                ss << "tt_sigmoid(" << x << ")";
-                break;
-            default: fail(TT_ERR_COMPILE, "internal: non-elementwise op in region");
-        }
-        ss << ";\n";
+        ss << "      const float v" << i << " = " << node_expr(nd, x, y) << ";\n";
     }
     for (size_t s = 0; s < nsto; ++s) {
         std::string val = r.is_copy ? ref(r.ext[0]) : "v" + std::to_string(r.stores[s]);
@@ -214,6 +340,18 @@ std::string generate_source(Plan& p) {
           "  if (x >= 0.0f) return 1.0f / (1.0f + tt_exp(-x));\n"
           "  const float ex = tt_exp(x);\n"
           "  return ex / (1.0f + ex);\n"
+          "}\n";
+    ss << "// hi/lo operand split of the 3xTF32 GEMM: hi = x with its low 13 mantissa bits cleared,\n"
+          "// lo = the same of x - hi (exact); NaN -> the canonical quiet NaN, +-inf -> (x, 0).\n";
+    ss << "__device__ __forceinline__ void tt_split(float x, float& hi, float& lo) {\n"
+          "  const unsigned u = __float_as_uint(x);\n"
+          "  if ((u & 0x7F800000u) != 0x7F800000u) {\n"
+          "    hi = __uint_as_float(u & 0xFFFFE000u);\n"
+          "    lo = __uint_as_float(__float_as_uint(__fsub_rn(x, hi)) & 0xFFFFE000u);\n"
+          "  } else {\n"
+          "    hi = (u & 0x7FFFFFFFu) > 0x7F800000u ? __uint_as_float(0x7FC00000u) : x;\n"
+          "    lo = 0.0f;\n"
+          "  }\n"
           "}\n\n";
     for (Launch& L : p.launches)
         if (L.type == LT_REGION) emit_region(ss, p, p.regions[static_cast<size_t>(L.region)]);

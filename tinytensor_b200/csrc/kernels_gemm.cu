@@ -17,7 +17,7 @@
 namespace ttb {
 
 int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
-                   void* stream);
+                   void* stream, const GemmSplitIO* io);
 bool gemm_tc_supported(const GemmDesc& d);
 int64_t gemm_tc_scratch_bytes(const GemmDesc& d);
 int gemm_tc_launch_count(const GemmDesc& d);
@@ -685,7 +685,7 @@ int gemm_launch_count(const GemmDesc& d) {
 }
 
 int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
-                void* stream) {
+                void* stream, const GemmSplitIO* io) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (d.M == 0 || d.N == 0 || d.batch == 0) return 0;
     A += d.a_off;
@@ -698,7 +698,7 @@ int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, voi
         }
         return 0;
     }
-    if (d.algo == ALGO_TC) return launch_gemm_tc(d, A, B, C, scratch, status, stream);
+    if (d.algo == ALGO_TC) return launch_gemm_tc(d, A, B, C, scratch, status, stream, io);
     if (d.algo == ALGO_SKINNY || d.algo == ALGO_SKINNY_T) return launch_skinny(d, A, B, C, scratch, st);
     if (d.algo == ALGO_SMALLK) {
         const int vec = d.N % 4 == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0 && d.c_sb % 4 == 0;

@@ -1000,29 +1000,38 @@ static int64_t operand_elems(int64_t R, int64_t K, int64_t s_b, int64_t batch) {
 }
 
 int64_t gemm_tc_scratch_bytes(const GemmDesc& d) {
-    const int64_t a = operand_elems(d.M, d.K, d.a_sb, d.batch), b = operand_elems(d.N, d.K, d.b_sb, d.batch);
+    const int64_t a = d.a_presplit ? 0 : operand_elems(d.M, d.K, d.a_sb, d.batch);
+    const int64_t b = d.b_presplit ? 0 : operand_elems(d.N, d.K, d.b_sb, d.batch);
     int64_t bytes = 2 * align256b(a * 4) + 2 * align256b(b * 4);
     if (d.ksplit > 1) bytes += align256b(d.batch * d.ksplit * d.M * d.N * 4);
     return bytes;
 }
 
 int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
-                   void* stream) {
+                   void* stream, const GemmSplitIO* io) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const OperandPlan ap = plan_operand(d.M, d.K, d.a_sb, d.batch);
     const OperandPlan bp = plan_operand(d.N, d.K, d.b_sb, d.batch);
-    const int64_t a_cap = align256b(operand_elems(d.M, d.K, d.a_sb, d.batch) * 4);
-    const int64_t b_cap = align256b(operand_elems(d.N, d.K, d.b_sb, d.batch) * 4);
+    if ((d.a_presplit || d.b_presplit) && (io == nullptr || d.batch != 1))
+        return static_cast<int>(cudaErrorInvalidValue);  // the scheduler never plans this
+    const int64_t a_cap = d.a_presplit ? 0 : align256b(operand_elems(d.M, d.K, d.a_sb, d.batch) * 4);
+    const int64_t b_cap = d.b_presplit ? 0 : align256b(operand_elems(d.N, d.K, d.b_sb, d.batch) * 4);
     char* s = static_cast<char*>(scratch);
-    float* ahi = reinterpret_cast<float*>(s);
-    float* alo = reinterpret_cast<float*>(s + a_cap);
-    float* bhi = reinterpret_cast<float*>(s + 2 * a_cap);
-    float* blo = reinterpret_cast<float*>(s + 2 * a_cap + b_cap);
+    // operand hi/lo: written into scratch by the pre-pass, or the producing region's copies
+    float* ahi = d.a_presplit ? const_cast<float*>(io->a_hi) : reinterpret_cast<float*>(s);
+    float* alo = d.a_presplit ? const_cast<float*>(io->a_lo) : reinterpret_cast<float*>(s + a_cap);
+    float* bhi = d.b_presplit ? const_cast<float*>(io->b_hi) : reinterpret_cast<float*>(s + 2 * a_cap);
+    float* blo = d.b_presplit ? const_cast<float*>(io->b_lo) : reinterpret_cast<float*>(s + 2 * a_cap + b_cap);
     float* partial = reinterpret_cast<float*>(s + 2 * a_cap + 2 * b_cap);
-    int rc = launch_split(A, ahi, alo, d.M, d.K, d.a_sm, d.a_sk, d.a_sb, ap, st);
-    if (rc) return rc;
-    rc = launch_split(B, bhi, blo, d.N, d.K, d.b_sn, d.b_sk, d.b_sb, bp, st);
-    if (rc) return rc;
+    int rc = 0;
+    if (!d.a_presplit) {
+        rc = launch_split(A, ahi, alo, d.M, d.K, d.a_sm, d.a_sk, d.a_sb, ap, st);
+        if (rc) return rc;
+    }
+    if (!d.b_presplit) {
+        rc = launch_split(B, bhi, blo, d.N, d.K, d.b_sn, d.b_sk, d.b_sb, bp, st);
+        if (rc) return rc;
+    }
     const int bk = d.bk == 16 ? 16 : 32;
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
     const int b_rows = d.pair ? 128 : BN;  // a pair CTA holds half of the 256-row B tile
@@ -1105,8 +1114,8 @@ int64_t gemm_tc_ctas(const GemmDesc& d) {
 
 int gemm_tc_launch_count(const GemmDesc& d) {
     int n = 1;
-    if (d.M && d.K) ++n;
-    if (d.N && d.K) ++n;
+    if (d.M && d.K && !d.a_presplit) ++n;
+    if (d.N && d.K && !d.b_presplit) ++n;
     if (d.ksplit > 1) ++n;
     return n;
 }

@@ -63,14 +63,31 @@ struct GemmDesc {
     int chunk_kb = 8;                      // tensor-core kernel: K blocks per TMEM chunk
     int bk = 32;                           // tensor-core kernel: K per pipeline stage (16 or 32)
     int pair = 0;                          // tensor-core kernel: 2-CTA (cta_group::2) 256x256 tiles
+    // Tensor-core kernel only: operands whose hi/lo copies the elementwise region that
+    // produced them already wrote (no pre-pass for them here).
+    int a_presplit = 0, b_presplit = 0;
 };
+// Device pointers of pre-split operands' hi/lo copies (compact K-major, rows padded to
+// round4(K) floats), null for operands split by the GEMM's own pre-pass.
+struct GemmSplitIO {
+    const float* a_hi = nullptr;
+    const float* a_lo = nullptr;
+    const float* b_hi = nullptr;
+    const float* b_lo = nullptr;
+};
+// Hi/lo operand copies of a row-major [R][C] matrix, one buffer: layout 0 = its own
+// layout [R][round4(C)] (hi, then lo), layout 1 = transposed [C][round4(R)] (hi, lo).
+// A GEMM reading the matrix along its rows (A = X or B = X^T) uses layout 0, one
+// reading it across (A = X^T or B = X) layout 1.
+int64_t split_copies_bytes(int64_t R, int64_t C, bool rows, bool t);
+int64_t split_copies_offset(int64_t R, int64_t C, bool rows, int layout, int lo);
 void plan_gemm(GemmDesc& d);  // picks the kernel variant for the shape/layout
 const char* gemm_algo_name(int algo);
 int64_t gemm_scratch_bytes(const GemmDesc& d);  // device scratch the chosen variant needs
 int gemm_launch_count(const GemmDesc& d);        // kernels one launch_gemm issues
 int64_t gemm_tc_ctas(const GemmDesc& d);         // CTAs of a tensor-core GEMM's main kernel (0 otherwise)
 int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, int* status,
-                void* stream);
+                void* stream, const GemmSplitIO* io = nullptr);
 // Sums split-K partials P[b][s][0..per) in split order into C[b*c_sb + i] and applies
 // the epilogue (deterministic).
 int launch_splitk_reduce(const float* P, float* C, int64_t per, int ksplit, int64_t batch, int64_t c_sb, int epilogue,
@@ -105,6 +122,12 @@ struct Region {
     std::string kernel;                 // generated kernel name
     int vec = 1, unroll = 4;
     int64_t grid = 0;
+    // Hi/lo operand copies of stores[copy_store] (an [copy_R][copy_C] matrix) for later
+    // tensor-core GEMMs, set by the scheduler; the kernel is then the tiled variant.
+    int copy_store = -1;
+    bool copy_rows = false, copy_t = false;
+    bool drop_f32 = false;              // that store has no other reader: its fp32 value is not written
+    int64_t copy_R = 0, copy_C = 0;
 };
 
 enum LaunchType { LT_REGION = 0, LT_REDUCE = 1, LT_GEMM = 2 };
@@ -120,6 +143,10 @@ struct Launch {
     int64_t scratch_bytes = 0;
     std::string label;                  // for profiles and the execution plan
     bool concurrent_next = false;       // this GEMM and the next launch (a GEMM) run side by side
+    BufRef split_ref;                   // region: its hi/lo operand copies (split_copies_bytes)
+    // GEMM: for a pre-split operand, the region launch that wrote its copies and the layout read
+    int a_split_src = -1, a_split_layout = 0;
+    int b_split_src = -1, b_split_layout = 0;
 };
 
 struct Slot {

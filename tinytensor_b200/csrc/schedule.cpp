@@ -40,6 +40,7 @@ bool is_contiguous(const Storage& s, const Shape& shape) {
 }
 
 int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+int64_t round4i(int64_t x) { return (x + 3) / 4 * 4; }
 
 // Access of `src` (shape `from`) broadcast to the iteration shape `to`.
 Access broadcast_access(const Storage& s, int node, const Shape& from, const Shape& to) {
@@ -100,6 +101,16 @@ void fold_gemm_epilogues(Graph& g, const std::vector<int>& out_pos) {
 }
 
 }  // namespace
+
+int64_t split_copies_bytes(int64_t R, int64_t C, bool rows, bool t) {
+    return (rows ? 2 * align256(R * round4i(C) * 4) : 0) + (t ? 2 * align256(C * round4i(R) * 4) : 0);
+}
+
+int64_t split_copies_offset(int64_t R, int64_t C, bool rows, int layout, int lo) {
+    const int64_t rcap = rows ? align256(R * round4i(C) * 4) : 0;
+    if (layout == 0) return lo ? rcap : 0;
+    return 2 * rcap + (lo ? align256(C * round4i(R) * 4) : 0);
+}
 
 Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
     Plan p;
@@ -716,6 +727,95 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         p.launches.push_back(L);
     }
 
+    // ---- hi/lo operand copies written by the producing region ----
+    // A tensor-core GEMM operand that is a whole 2-D matrix stored by an elementwise
+    // region, read as it is along K (A = X, or B = X^T) or across K (A = X^T, or B = X),
+    // is not split by a pre-pass of its own: the region writes the hi/lo copies in the
+    // layout(s) its GEMM readers use, from the values it has in registers (a tiled
+    // kernel; the transposed copies go out through shared memory in 128-B runs).  When
+    // nothing else reads the matrix, its fp32 value is not stored at all.  This replaces
+    // a re-read of the matrix (and its fp32 write) per reading GEMM.
+    std::vector<char> dropped(g.nodes.size(), 0);
+    if (opt.gemm_epilogue) {
+        std::map<int, std::pair<int, int>> store_of;  // node -> (region launch, store index)
+        for (size_t s = 0; s < p.launches.size(); ++s) {
+            const Launch& L = p.launches[s];
+            if (L.type != LT_REGION) continue;
+            const Region& r = p.regions[static_cast<size_t>(L.region)];
+            if (r.is_copy || r.stores.empty()) continue;
+            for (size_t j = 0; j < r.stores.size(); ++j) {
+                const Shape& sh = g.nodes[static_cast<size_t>(r.stores[j])].shape;
+                if (sh.size() == 2 && sh[0] > 1 && sh[1] > 1 && sh == r.shape)
+                    store_of[r.stores[j]] = {static_cast<int>(s), static_cast<int>(j)};
+            }
+        }
+        for (size_t c = 0; c < p.launches.size(); ++c) {
+            Launch& L = p.launches[c];
+            if (L.type != LT_GEMM || L.gd.algo != 2 || L.gd.batch != 1) continue;
+            GemmDesc& d = L.gd;
+            for (int k = 0; k < 2; ++k) {
+                const int node = k == 0 ? L.in_node : L.in_node2;
+                auto it = store_of.find(node);
+                if (it == store_of.end() || it->second.first >= static_cast<int>(c)) continue;
+                Launch& P = p.launches[static_cast<size_t>(it->second.first)];
+                Region& pr = p.regions[static_cast<size_t>(P.region)];
+                if (pr.copy_store >= 0 && pr.copy_store != it->second.second) continue;  // one copied store per region
+                const Shape& sh = g.nodes[static_cast<size_t>(node)].shape;
+                const int64_t pm = sh[0], pn = sh[1];  // X: [pm][pn], row stride pn
+                int layout = -1;
+                if (k == 0 && d.a_off == 0) {  // A[m][k]; its K-major copy is [M][round4(K)]
+                    if (d.a_sk == 1 && d.a_sm == pn && d.M == pm && d.K == pn) layout = 0;       // A = X
+                    else if (d.a_sm == 1 && d.a_sk == pn && d.M == pn && d.K == pm) layout = 1;  // A = X^T
+                } else if (k == 1 && d.b_off == 0) {  // B[k][n]; its K-major copy is [N][round4(K)]
+                    if (d.b_sk == 1 && d.b_sn == pn && d.N == pm && d.K == pn) layout = 0;       // B = X^T
+                    else if (d.b_sn == 1 && d.b_sk == pn && d.N == pn && d.K == pm) layout = 1;  // B = X
+                }
+                if (layout < 0) continue;
+                pr.copy_store = it->second.second;
+                pr.copy_R = pm;
+                pr.copy_C = pn;
+                if (layout == 0) pr.copy_rows = true;
+                else pr.copy_t = true;
+                if (k == 0) {
+                    d.a_presplit = 1;
+                    L.a_split_src = it->second.first;
+                    L.a_split_layout = layout;
+                } else {
+                    d.b_presplit = 1;
+                    L.b_split_src = it->second.first;
+                    L.b_split_layout = layout;
+                }
+                std::ostringstream lb;
+                lb << " (" << (k == 0 ? "A" : "B") << " hi/lo from [" << it->second.first << "])";
+                L.label += lb.str();
+            }
+            L.scratch_bytes = gemm_scratch_bytes(d);
+        }
+        // a copied matrix whose only readers take the copies is not stored in fp32
+        for (Launch& L : p.launches) {
+            if (L.type != LT_REGION) continue;
+            Region& r = p.regions[static_cast<size_t>(L.region)];
+            if (r.copy_store < 0) continue;
+            const int q = r.stores[static_cast<size_t>(r.copy_store)];
+            bool other = out_pos.size() > static_cast<size_t>(q) && out_pos[static_cast<size_t>(q)] >= 0;
+            for (const Launch& U : p.launches) {
+                if (U.type == LT_REGION) {
+                    for (const Access& a : p.regions[static_cast<size_t>(U.region)].ext_access)
+                        other |= !a.imm && a.node == q;
+                } else if (U.type == LT_REDUCE) {
+                    other |= U.in_node == q;
+                } else {
+                    other |= (U.in_node == q && !U.gd.a_presplit) || (U.in_node2 == q && !U.gd.b_presplit);
+                }
+            }
+            r.drop_f32 = !other;
+            if (r.drop_f32) dropped[static_cast<size_t>(q)] = 1;
+            L.label += r.copy_rows && r.copy_t ? " (writes hi/lo of X and X^T" : r.copy_rows ? " (writes hi/lo of X"
+                                                                                             : " (writes hi/lo of X^T";
+            L.label += r.drop_f32 ? ", not X)" : ")";
+        }
+    }
+
     // ---- concurrent GEMM pairs ----
     // Two adjacent tensor-core GEMM launches, the second neither reading the first's
     // output nor writing what the first reads, each of at most four waves of CTAs, run
@@ -765,6 +865,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
     for (size_t u = 0; u < units.size(); ++u)
         for (int w : units[u].writes) {
             if (p.root_ref[static_cast<size_t>(w)].kind == BK_OUTPUT) continue;
+            if (dropped[static_cast<size_t>(w)]) continue;  // fp32 value never stored (copies only)
             Life l{w, step_of_unit[u], step_of_unit[u],
                    numel(g.nodes[static_cast<size_t>(w)].shape) * static_cast<int64_t>(sizeof(float))};
             life_of[w] = lives.size();
@@ -778,6 +879,21 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
     for (size_t s = 0; s < p.launches.size(); ++s)
         if (p.launches[s].scratch_bytes > 0)
             lives.push_back(Life{-1 - static_cast<int>(s), plan_step[s], plan_step[s], p.launches[s].scratch_bytes});
+    // a region's hi/lo operand copies: from the region to its last GEMM reader
+    const int nlaunch = static_cast<int>(p.launches.size());
+    for (size_t s = 0; s < p.launches.size(); ++s) {
+        const Launch& L = p.launches[s];
+        if (L.type != LT_REGION || p.regions[static_cast<size_t>(L.region)].copy_store < 0) continue;
+        const Region& r = p.regions[static_cast<size_t>(L.region)];
+        int last = plan_step[s];
+        for (size_t c = 0; c < p.launches.size(); ++c) {
+            const Launch& C = p.launches[c];
+            if (C.a_split_src == static_cast<int>(s) || C.b_split_src == static_cast<int>(s))
+                last = std::max(last, plan_step[c]);
+        }
+        lives.push_back(Life{-1 - nlaunch - static_cast<int>(s), plan_step[s], last,
+                             split_copies_bytes(r.copy_R, r.copy_C, r.copy_rows, r.copy_t)});
+    }
     p.num_intermediates = lives.size();
     for (const Life& l : lives) p.total_alloc_bytes += l.bytes;
     for (size_t s = 0; s <= p.launches.size(); ++s) {
@@ -833,7 +949,8 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         r.kind = BK_ARENA;
         r.offset = p.slots[static_cast<size_t>(l.slot)].offset;
         if (l.root >= 0) p.root_ref[static_cast<size_t>(l.root)] = r;
-        else p.launches[static_cast<size_t>(-1 - l.root)].scratch_ref = r;
+        else if (-1 - l.root < nlaunch) p.launches[static_cast<size_t>(-1 - l.root)].scratch_ref = r;
+        else p.launches[static_cast<size_t>(-1 - nlaunch - l.root)].split_ref = r;
     }
     p.stage_in_offset = off;
     for (int k : g.inputs) {
@@ -901,6 +1018,9 @@ std::string plan_text(const Plan& p) {
             const Region& r = p.regions[static_cast<size_t>(L.region)];
             ss << " kernel=" << r.kernel << " vec=" << r.vec << " grid=" << r.grid << " ->";
             for (const BufRef& b : r.store_ref) ss << " " << kind_name(b.kind) << ":" << (b.kind == BK_ARENA ? b.offset : b.index);
+            if (r.copy_store >= 0)
+                ss << " copies=" << split_copies_bytes(r.copy_R, r.copy_C, r.copy_rows, r.copy_t) << "@"
+                   << L.split_ref.offset;
         } else {
             ss << " ->" << " " << kind_name(L.out_ref.kind) << ":"
                << (L.out_ref.kind == BK_ARENA ? L.out_ref.offset : L.out_ref.index);
