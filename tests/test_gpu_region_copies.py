@@ -99,3 +99,46 @@ def test_special_values_survive_the_copies(cache_dir):
     keep = np.ones(256, bool)
     keep[[3, 9]] = False
     assert_norm(got[keep], O.matmul(a[keep], y), GEMM_FROB_RTOL)
+
+
+@pytest.mark.parametrize("bshape", [(1, 520), (300, 1), ()])
+def test_tiled_region_with_broadcast_operands(bshape, cache_dir):
+    """The tiled region reads broadcast operands (a row vector, a column vector, a
+    scalar constant) with their own strides; X = relu(a + b) * 0.5 feeds A = X^T."""
+    rng = np.random.default_rng(47 + len(bshape))
+    a = _data(rng, (300, 520), 1.0)
+    y = _data(rng, (300, 96), 1 / np.sqrt(300))
+    g = tt.Graph()
+    na, ny = g.input([300, 520]), g.input([300, 96])
+    feed = {na: a, ny: y}
+    if bshape:
+        b = _data(rng, bshape, 1.0)
+        nb = g.input(list(bshape))
+        feed[nb] = b
+        x = tt.relu(na + nb) * 0.5
+        xr = O.binary(O.MUL, O.unary(O.RELU, O.binary(O.ADD, a, b)), np.float32(0.5))
+    else:
+        x = tt.relu(na + 0.25) * 0.5
+        xr = O.binary(O.MUL, O.unary(O.RELU, O.binary(O.ADD, a, np.float32(0.25))), np.float32(0.5))
+    prog = tt.compile(g, outputs=[tt.transpose(x, 0, 1) @ ny], cache_dir=cache_dir)
+    assert "(writes hi/lo of X^T, not X)" in prog.execution_plan()
+    got = prog.run(feed).numpy()
+    assert_norm(got, O.matmul(np.ascontiguousarray(xr.T), y), GEMM_FROB_RTOL)
+
+
+def test_region_with_two_stores_copies_one(cache_dir):
+    """A region storing two matrices (u = a * b, an output, and v = u + a, read by a
+    GEMM): v's copies are written, u's fp32 store stays bit-exact."""
+    rng = np.random.default_rng(53)
+    a, b = _data(rng, (512, 384), 1.0), _data(rng, (512, 384), 1.0)
+    y = _data(rng, (384, 200), 1 / np.sqrt(384))
+    g = tt.Graph()
+    na, nb, ny = g.input([512, 384]), g.input([512, 384]), g.input([384, 200])
+    u = na * nb
+    v = u + na
+    prog = tt.compile(g, outputs=[u, v @ ny], cache_dir=cache_dir)
+    assert "(writes hi/lo of X, not X)" in prog.execution_plan()
+    gu, gv = (t.numpy() for t in prog.run({na: a, nb: b, ny: y}))
+    ur = O.binary(O.MUL, a, b)
+    assert_bitexact(gu, ur)
+    assert_norm(gv, O.matmul(O.binary(O.ADD, ur, a), y), GEMM_FROB_RTOL)
