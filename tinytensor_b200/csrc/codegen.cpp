@@ -57,11 +57,14 @@ int64_t round4c(int64_t x) { return (x + 3) / 4 * 4; }
 // A region that also writes hi/lo operand copies of its stored [R][C] matrix X (for
 // tensor-core GEMMs that read X without a pre-pass of their own).  A CTA computes one
 // 32-row x 128-column tile: each warp takes rows w, w+8, w+16, w+24 with a float4 of
-// columns per lane (coalesced loads, fp32 stores and row-layout copies), parks the
-// tile in shared memory (row pitch 129 floats: conflict-free column reads), then each
-// warp writes 16 columns of the transposed copies with lane = row (128-B runs).  Tiles
-// are numbered rows first, so the CTAs resident together write neighbouring runs of
-// each transposed row; one CTA per tile (the hardware balances the SMs).
+// columns per lane, issuing the four rows' loads before any arithmetic (so they are in
+// flight together), then stores fp32 values and row-layout copies (coalesced) and parks
+// the tile in shared memory; then each lane reads 4-column float4 chunks of its row
+// (lane = row) and writes the transposed copies, one 128-B run per column and warp.
+// The tile pitch of 132 floats keeps both the float4 stores and the float4 column-chunk
+// reads at the minimum four shared-memory wavefronts.  Tiles are numbered rows first,
+// so the CTAs resident together write neighbouring runs of each transposed row; one
+// CTA per tile (the hardware balances the SMs).
 static void emit_region_tiled(std::ostringstream& ss, const Plan& p, Region& r) {
     const Graph& g = p.g;
     const size_t next = r.ext.size(), nsto = r.store_ref.size();
@@ -85,90 +88,103 @@ static void emit_region_tiled(std::ostringstream& ss, const Plan& p, Region& r) 
     for (size_t k = 0; k < nsto; ++k) ss << (next + k ? ", " : "") << "float* __restrict__ y" << k;
     ss << ", float* __restrict__ ch, float* __restrict__ cl, float* __restrict__ th, float* __restrict__ tl) {\n";
     ss << "  typedef " << it << " I;\n";
-    ss << "  __shared__ float tile[32][129];\n";
+    if (r.copy_t) ss << "  __shared__ __align__(16) float tile[32][132];\n";
     ss << "  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;\n";
-    ss << "  {\n    const I t = blockIdx.x;\n";
-    ss << "    const I r0 = (t % " << tiles_r << ") * 32, c0 = (t / " << tiles_r << ") * 128;\n";
-    ss << "    const I c = c0 + 4 * lane;\n";
-    ss << "#pragma unroll\n    for (int i = 0; i < 4; ++i) {\n";
-    ss << "      const I rr = r0 + w + 8 * i;\n";
-    ss << "      const bool rin = rr < (I)" << R << ", full = rin && c + 3 < (I)" << C << ";\n";
-    // loads: a<e>[l] for the four columns c..c+3 of row rr (0 outside X)
+    ss << "  const I t = blockIdx.x;\n";
+    ss << "  const I r0 = (t % " << tiles_r << ") * 32, c0 = (t / " << tiles_r << ") * 128;\n";
+    ss << "  const I c = c0 + 4 * lane;\n";
+    // loads of the four rows: a<e>[i][l] (0 outside X); scalar per row when broadcast along columns
     for (size_t e = 0; e < next; ++e) {
         const Access& a = r.ext_access[e];
         if (a.imm) {
-            ss << "      const float a" << e << " = " << flit(a.value) << ";\n";
+            ss << "  const float a" << e << " = " << flit(a.value) << ";\n";
             continue;
         }
+        ss << (a.strides[1] == 0 ? "  float a" + std::to_string(e) + "[4];\n"
+                                 : "  float a" + std::to_string(e) + "[4][4];\n");
+    }
+    ss << "#pragma unroll\n  for (int i = 0; i < 4; ++i) {\n";
+    ss << "    const I rr = r0 + w + 8 * i;\n";
+    ss << "    const bool rin = rr < (I)" << R << ", full = rin && c + 3 < (I)" << C << ";\n";
+    for (size_t e = 0; e < next; ++e) {
+        const Access& a = r.ext_access[e];
+        if (a.imm) continue;
         const int64_t sr = a.strides[0], sc = a.strides[1];
         std::ostringstream base;
         base << a.offset << " + rr * (I)" << sr;
         if (sc == 0) {
-            ss << "      const float a" << e << " = rin ? __ldg(x" << e << " + (" << base.str() << ")) : 0.0f;\n";
+            ss << "    a" << e << "[i] = rin ? __ldg(x" << e << " + (" << base.str() << ")) : 0.0f;\n";
         } else if (sc == 1 && sr % 4 == 0 && a.offset % 4 == 0 && C % 4 == 0) {
-            ss << "      float a" << e << "[4] = {0.0f, 0.0f, 0.0f, 0.0f};\n";
-            ss << "      if (full) { const float4 q = __ldg(reinterpret_cast<const float4*>(x" << e << " + (" << base.str()
-               << " + c))); a" << e << "[0] = q.x; a" << e << "[1] = q.y; a" << e << "[2] = q.z; a" << e << "[3] = q.w; }\n";
+            ss << "    { float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);\n";
+            ss << "      if (full) q = __ldg(reinterpret_cast<const float4*>(x" << e << " + (" << base.str() << " + c)));\n";
+            ss << "      a" << e << "[i][0] = q.x; a" << e << "[i][1] = q.y; a" << e << "[i][2] = q.z; a" << e
+               << "[i][3] = q.w; }\n";
         } else {
-            ss << "      float a" << e << "[4];\n";
-            ss << "#pragma unroll\n      for (int l = 0; l < 4; ++l) a" << e << "[l] = (rin && c + l < (I)" << C
+            ss << "#pragma unroll\n    for (int l = 0; l < 4; ++l) a" << e << "[i][l] = (rin && c + l < (I)" << C
                << ") ? __ldg(x" << e << " + (" << base.str() << " + (c + l) * (I)" << sc << ")) : 0.0f;\n";
         }
     }
+    ss << "  }\n";
     auto ref = [&](int node) -> std::string {
         auto itx = std::find(r.ext.begin(), r.ext.end(), node);
         if (itx != r.ext.end()) {
             const size_t e = static_cast<size_t>(itx - r.ext.begin());
             const Access& a = r.ext_access[e];
-            const bool lanes = !a.imm && a.strides[1] != 0;
-            return "a" + std::to_string(e) + (lanes ? "[l]" : "");
+            if (a.imm) return "a" + std::to_string(e);
+            return "a" + std::to_string(e) + (a.strides[1] != 0 ? "[i][l]" : "[i]");
         }
         return "v" + std::to_string(node);
     };
-    for (size_t k = 0; k < nsto; ++k) ss << "      float o" << k << "[4];\n";
-    ss << "#pragma unroll\n      for (int l = 0; l < 4; ++l) {\n";
+    ss << "#pragma unroll\n  for (int i = 0; i < 4; ++i) {\n";
+    ss << "    const I rr = r0 + w + 8 * i;\n";
+    ss << "    const bool rin = rr < (I)" << R << ", full = rin && c + 3 < (I)" << C << ";\n";
+    for (size_t k = 0; k < nsto; ++k) ss << "    float o" << k << "[4];\n";
+    ss << "#pragma unroll\n    for (int l = 0; l < 4; ++l) {\n";
     for (int i : r.nodes) {
         const Node& nd = g.nodes[static_cast<size_t>(i)];
-        ss << "        const float v" << i << " = "
+        ss << "      const float v" << i << " = "
            << node_expr(nd, ref(nd.in[0]), nd.in.size() > 1 ? ref(nd.in[1]) : "") << ";\n";
     }
-    for (size_t k = 0; k < nsto; ++k) ss << "        o" << k << "[l] = v" << r.stores[k] << ";\n";
-    ss << "      }\n";
+    for (size_t k = 0; k < nsto; ++k) ss << "      o" << k << "[l] = v" << r.stores[k] << ";\n";
+    ss << "    }\n";
     // fp32 stores of [R][C] matrices (row stride C)
     for (size_t k = 0; k < nsto; ++k) {
         if (k == cs && r.drop_f32) continue;
         if (C % 4 == 0)
-            ss << "      if (full) *reinterpret_cast<float4*>(y" << k << " + rr * (I)" << C << " + c) = make_float4(o" << k
-               << "[0], o" << k << "[1], o" << k << "[2], o" << k << "[3]);\n      else";
-        ss << "      if (rin) { for (int l = 0; l < 4; ++l) if (c + l < (I)" << C << ") y" << k << "[rr * (I)" << C
+            ss << "    if (full) *reinterpret_cast<float4*>(y" << k << " + rr * (I)" << C << " + c) = make_float4(o" << k
+               << "[0], o" << k << "[1], o" << k << "[2], o" << k << "[3]);\n    else";
+        ss << "    if (rin) { for (int l = 0; l < 4; ++l) if (c + l < (I)" << C << ") y" << k << "[rr * (I)" << C
            << " + c + l] = o" << k << "[l]; }\n";
     }
     if (r.copy_rows) {  // copies in X's layout, row pitch round4(C)
-        ss << "      if (rin) {\n        float4 h, q;\n";
-        ss << "        tt_split(o" << cs << "[0], h.x, q.x); tt_split(o" << cs << "[1], h.y, q.y);\n";
-        ss << "        tt_split(o" << cs << "[2], h.z, q.z); tt_split(o" << cs << "[3], h.w, q.w);\n";
-        ss << "        if (c + 3 < (I)" << C << ") { *reinterpret_cast<float4*>(ch + rr * (I)" << Cp
+        ss << "    if (rin) {\n      float4 h, q;\n";
+        ss << "      tt_split(o" << cs << "[0], h.x, q.x); tt_split(o" << cs << "[1], h.y, q.y);\n";
+        ss << "      tt_split(o" << cs << "[2], h.z, q.z); tt_split(o" << cs << "[3], h.w, q.w);\n";
+        ss << "      if (c + 3 < (I)" << C << ") { *reinterpret_cast<float4*>(ch + rr * (I)" << Cp
            << " + c) = h; *reinterpret_cast<float4*>(cl + rr * (I)" << Cp << " + c) = q; }\n";
-        ss << "        else { const float hv[4] = {h.x, h.y, h.z, h.w}, lv[4] = {q.x, q.y, q.z, q.w};\n";
-        ss << "          for (int l = 0; l < 4; ++l) if (c + l < (I)" << C << ") { ch[rr * (I)" << Cp
+        ss << "      else { const float hv[4] = {h.x, h.y, h.z, h.w}, lv[4] = {q.x, q.y, q.z, q.w};\n";
+        ss << "        for (int l = 0; l < 4; ++l) if (c + l < (I)" << C << ") { ch[rr * (I)" << Cp
            << " + c + l] = hv[l]; cl[rr * (I)" << Cp << " + c + l] = lv[l]; } }\n";
-        ss << "      }\n";
+        ss << "    }\n";
     }
-    if (r.copy_t) {
-        ss << "      tile[w + 8 * i][4 * lane] = o" << cs << "[0]; tile[w + 8 * i][4 * lane + 1] = o" << cs << "[1];\n";
-        ss << "      tile[w + 8 * i][4 * lane + 2] = o" << cs << "[2]; tile[w + 8 * i][4 * lane + 3] = o" << cs << "[3];\n";
-    }
-    ss << "    }\n";
+    if (r.copy_t)
+        ss << "    *reinterpret_cast<float4*>(&tile[w + 8 * i][4 * lane]) = make_float4(o" << cs << "[0], o" << cs
+           << "[1], o" << cs << "[2], o" << cs << "[3]);\n";
+    ss << "  }\n";
     if (r.copy_t) {  // transposed copies [C][round4(R)]: lane = row, one 128-B run per column
-        ss << "    __syncthreads();\n";
-        ss << "#pragma unroll 4\n    for (int j = 0; j < 16; ++j) {\n";
-        ss << "      const I cc = c0 + w * 16 + j, rr = r0 + lane;\n";
+        ss << "  __syncthreads();\n";
+        ss << "  const I rr = r0 + lane;\n";
+        ss << "#pragma unroll\n  for (int j = 0; j < 4; ++j) {\n";
+        ss << "    const float4 q = *reinterpret_cast<const float4*>(&tile[lane][w * 16 + 4 * j]);\n";
+        ss << "    const float qv[4] = {q.x, q.y, q.z, q.w};\n";
+        ss << "#pragma unroll\n    for (int u = 0; u < 4; ++u) {\n";
+        ss << "      const I cc = c0 + w * 16 + 4 * j + u;\n";
         ss << "      if (cc < (I)" << C << " && rr < (I)" << R << ") {\n";
-        ss << "        float h, q;\n        tt_split(tile[lane][w * 16 + j], h, q);\n";
-        ss << "        th[cc * (I)" << Rp << " + rr] = h;\n        tl[cc * (I)" << Rp << " + rr] = q;\n      }\n";
-        ss << "    }\n    __syncthreads();\n";
+        ss << "        float h, l;\n        tt_split(qv[u], h, l);\n";
+        ss << "        th[cc * (I)" << Rp << " + rr] = h;\n        tl[cc * (I)" << Rp << " + rr] = l;\n      }\n";
+        ss << "    }\n  }\n";
     }
-    ss << "  }\n}\n\n";
+    ss << "}\n\n";
 }
 
 static void emit_region(std::ostringstream& ss, const Plan& p, Region& r) {
