@@ -155,9 +155,10 @@ def run_b200(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     peaks, peak_src = load_peaks()
 
-    rows = GLOBAL_BATCH // world
+    batch = args.batch
+    rows = batch // world
     r0 = rank * rows
-    x, t, w = mlp_data()
+    x, t, w = mlp_data(rows=batch)
     xs, ts = x[r0:r0 + rows], t[r0:r0 + rows]
     g, (X, T, W1, W2, W3), loss = mlp_graph(tt, rows)
     prog = tt.compile_gradients(g, loss, [W1, W2, W3], device=local)
@@ -265,9 +266,9 @@ def run_b200(args):
     total_prof = sum(t for _, t in prof)
     step_profile = [{"launch": lbl, "ms": round(t, 4), "share": round(t / total_prof, 4)}
                     for lbl, t in sorted(prof, key=lambda p: -p[1])[:10]]
-    step_flops = mlp_flops(GLOBAL_BATCH)
+    step_flops = mlp_flops(batch)
     out = {
-        "metric": "MLP DP SGD step/s (1024-4096-4096-10, global batch 32768)",
+        "metric": f"MLP DP SGD step/s (1024-4096-4096-10, global batch {batch})",
         "value": round(1000.0 / ms, 4),
         "unit": "step/s",
         "n_gpus": world,
@@ -279,7 +280,7 @@ def run_b200(args):
         "vs_baseline": None,
         "dtype": "f32 (3xTF32 tensor-core GEMM, fp32 accumulate)",
         "data": "synthetic: X,T ~ N(0,1) seed 4; Xavier-uniform weights seed 4",
-        "config": {"workload": "mlp_dp_sgd_step", "model": "MLP 1024-4096-4096-10 MSE", "global_batch": GLOBAL_BATCH,
+        "config": {"workload": "mlp_dp_sgd_step", "model": "MLP 1024-4096-4096-10 MSE", "global_batch": batch,
                    "per_gpu_batch": rows, "lr": LR, "parallelism": f"dp{world}",
                    "l2": "inputs larger than L2 (activations 512 MiB at N=1, weights 84 MB)",
                    "tflops_per_step": round(step_flops / 1e12, 4)},
@@ -293,7 +294,7 @@ def run_b200(args):
     }
     if world == 1 and not args.no_components:
         out["components"] = components(tt, torch, args, peaks, peak_src)
-    if rank == 0 and not args.no_cpu_baseline and world == 1:
+    if rank == 0 and not args.no_cpu_baseline and world == 1 and batch == GLOBAL_BATCH:
         out["cpu_baseline"] = cpu_baseline(args, sample_rows=64)
     if dist is not None:
         dist.barrier()
@@ -511,6 +512,8 @@ def main():
     ap.add_argument("--workload", default="mlp", choices=["mlp", "gemm", "elementwise", "reduce"],
                     help="mlp: the headline step; the others time one compiled program (profiling cases)")
     ap.add_argument("--size", default=None, help="gemm: M,N,K; elementwise: n (an n x n chain); reduce: R,C")
+    ap.add_argument("--batch", type=int, default=GLOBAL_BATCH,
+                    help="mlp: global batch (the headline is 32768; smaller values are profiling cases)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
