@@ -52,6 +52,14 @@ std::string node_expr(const Node& nd, const std::string& x, const std::string& y
 
 int64_t round4c(int64_t x) { return (x + 3) / 4 * 4; }
 
+// Ext index of the role (1 = A, 2 = B) operand of the small-K matmul node `mm`.
+size_t mm_operand(const Region& r, int mm, int role) {
+    for (size_t e = 0; e < r.ext.size(); ++e)
+        if (r.ext_access[e].mm == mm && r.ext_access[e].role == role) return e;
+    fail(TT_ERR_COMPILE, "internal: small-K matmul operand missing");
+    return 0;
+}
+
 }  // namespace
 
 // A region that also writes hi/lo operand copies of its stored [R][C] matrix X (for
@@ -76,14 +84,20 @@ static void emit_region_tiled(std::ostringstream& ss, const Plan& p, Region& r) 
     int64_t maxoff = std::max(R * Cp, C * Rp);
     for (size_t e = 0; e < next; ++e) {
         const Access& a = r.ext_access[e];
-        if (!a.imm) maxoff = std::max(maxoff, a.offset + (R - 1) * a.strides[0] + (C - 1) * a.strides[1] + 1);
+        if (!a.imm)
+            maxoff = std::max(maxoff, a.offset + (R - 1) * a.strides[0] + (C - 1) * a.strides[1] +
+                                          (a.kcount > 0 ? (a.kcount - 1) * a.kstride : 0) + 1);
     }
     const char* it = maxoff < (1LL << 31) - 1024 ? "int" : "long long";
     const size_t cs = static_cast<size_t>(r.copy_store);
     ss << "// region " << r.kernel << ": fused over " << shape_str(r.shape) << ", tiled, hi/lo copies of store " << cs
        << (r.copy_rows ? " [R][C]" : "") << (r.copy_t ? " [C][R]" : "") << (r.drop_f32 ? ", its fp32 not stored" : "")
        << "\n";
-    ss << "extern \"C\" __global__ void __launch_bounds__(256) " << r.kernel << "(";
+    // A region that forms a small-K product would hold B's values for all four rows in
+    // registers (80 per thread, 3 CTAs per SM); capping it at 64 keeps 4 CTAs resident.
+    bool has_mm = false;
+    for (int i : r.nodes) has_mm |= g.nodes[static_cast<size_t>(i)].inline_mm;
+    ss << "extern \"C\" __global__ void __launch_bounds__(256" << (has_mm ? ", 4" : "") << ") " << r.kernel << "(";
     for (size_t e = 0; e < next; ++e) ss << (e ? ", " : "") << "const float* __restrict__ x" << e;
     for (size_t k = 0; k < nsto; ++k) ss << (next + k ? ", " : "") << "float* __restrict__ y" << k;
     ss << ", float* __restrict__ ch, float* __restrict__ cl, float* __restrict__ th, float* __restrict__ tl) {\n";
@@ -96,6 +110,7 @@ static void emit_region_tiled(std::ostringstream& ss, const Plan& p, Region& r) 
     // loads of the four rows: a<e>[i][l] (0 outside X); scalar per row when broadcast along columns
     for (size_t e = 0; e < next; ++e) {
         const Access& a = r.ext_access[e];
+        if (a.role != 0) continue;  // small-K matmul operands are read where the product is formed
         if (a.imm) {
             ss << "  const float a" << e << " = " << flit(a.value) << ";\n";
             continue;
@@ -108,7 +123,7 @@ static void emit_region_tiled(std::ostringstream& ss, const Plan& p, Region& r) 
     ss << "    const bool rin = rr < (I)" << R << ", full = rin && c + 3 < (I)" << C << ";\n";
     for (size_t e = 0; e < next; ++e) {
         const Access& a = r.ext_access[e];
-        if (a.imm) continue;
+        if (a.imm || a.role != 0) continue;
         const int64_t sr = a.strides[0], sc = a.strides[1];
         std::ostringstream base;
         base << a.offset << " + rr * (I)" << sr;
@@ -126,22 +141,61 @@ static void emit_region_tiled(std::ostringstream& ss, const Plan& p, Region& r) 
     }
     ss << "  }\n";
     auto ref = [&](int node) -> std::string {
-        auto itx = std::find(r.ext.begin(), r.ext.end(), node);
-        if (itx != r.ext.end()) {
-            const size_t e = static_cast<size_t>(itx - r.ext.begin());
+        for (size_t e = 0; e < next; ++e) {
+            if (r.ext[e] != node || r.ext_access[e].role != 0) continue;
             const Access& a = r.ext_access[e];
             if (a.imm) return "a" + std::to_string(e);
             return "a" + std::to_string(e) + (a.strides[1] != 0 ? "[i][l]" : "[i]");
         }
         return "v" + std::to_string(node);
     };
+    // small-K matmul operands: the tile's 32 rows of A and 128 columns of B staged in shared
+    // memory once per CTA (read in the order that is contiguous in global memory)
+    bool staged = false;
+    for (int i : r.nodes) {
+        if (!g.nodes[static_cast<size_t>(i)].inline_mm) continue;
+        const size_t ea = mm_operand(r, i, 1), eb = mm_operand(r, i, 2);
+        const Access& a = r.ext_access[ea];
+        const Access& b = r.ext_access[eb];
+        const int64_t K = a.kcount;
+        ss << "  __shared__ float sa" << i << "[32][" << K << "];\n";
+        ss << "  __shared__ __align__(16) float sb" << i << "[" << K << "][128];\n";
+        ss << "  for (int e = threadIdx.x; e < " << 32 * K << "; e += 256) {\n";
+        if (a.kstride == 1) ss << "    const int q = e / " << K << ", k = e % " << K << ";\n";
+        else ss << "    const int k = e / 32, q = e % 32;\n";
+        ss << "    sa" << i << "[q][k] = r0 + q < (I)" << R << " ? __ldg(x" << ea << " + (" << a.offset << " + (r0 + q) * (I)"
+           << a.strides[0] << " + (I)k * " << a.kstride << ")) : 0.0f;\n  }\n";
+        ss << "  for (int e = threadIdx.x; e < " << 128 * K << "; e += 256) {\n";
+        if (b.kstride == 1) ss << "    const int q = e / " << K << ", k = e % " << K << ";\n";
+        else ss << "    const int k = e / 128, q = e % 128;\n";
+        ss << "    sb" << i << "[k][q] = c0 + q < (I)" << C << " ? __ldg(x" << eb << " + (" << b.offset << " + (c0 + q) * (I)"
+           << b.strides[1] << " + (I)k * " << b.kstride << ")) : 0.0f;\n  }\n";
+        staged = true;
+    }
+    if (staged) ss << "  __syncthreads();\n";
     ss << "#pragma unroll\n  for (int i = 0; i < 4; ++i) {\n";
     ss << "    const I rr = r0 + w + 8 * i;\n";
     ss << "    const bool rin = rr < (I)" << R << ", full = rin && c + 3 < (I)" << C << ";\n";
+    for (int i : r.nodes) {  // this row's products for the lane's four columns
+        if (!g.nodes[static_cast<size_t>(i)].inline_mm) continue;
+        const int64_t K = r.ext_access[mm_operand(r, i, 1)].kcount;
+        ss << "    float pm" << i << "[4] = {0.0f, 0.0f, 0.0f, 0.0f};\n";
+        ss << "#pragma unroll\n    for (int k = 0; k < " << K << "; ++k) {  // one sequential fmaf chain per element\n";
+        ss << "      const float av = sa" << i << "[w + 8 * i][k];\n";
+        ss << "      const float4 bv = *reinterpret_cast<const float4*>(&sb" << i << "[k][4 * lane]);\n";
+        ss << "      pm" << i << "[0] = fmaf(av, bv.x, pm" << i << "[0]); pm" << i << "[1] = fmaf(av, bv.y, pm" << i
+           << "[1]);\n";
+        ss << "      pm" << i << "[2] = fmaf(av, bv.z, pm" << i << "[2]); pm" << i << "[3] = fmaf(av, bv.w, pm" << i
+           << "[3]);\n    }\n";
+    }
     for (size_t k = 0; k < nsto; ++k) ss << "    float o" << k << "[4];\n";
     ss << "#pragma unroll\n    for (int l = 0; l < 4; ++l) {\n";
     for (int i : r.nodes) {
         const Node& nd = g.nodes[static_cast<size_t>(i)];
+        if (nd.inline_mm) {  // formed above: one sequential fmaf chain over k per element
+            ss << "      const float v" << i << " = pm" << i << "[l];\n";
+            continue;
+        }
         ss << "      const float v" << i << " = "
            << node_expr(nd, ref(nd.in[0]), nd.in.size() > 1 ? ref(nd.in[1]) : "") << ";\n";
     }
@@ -237,7 +291,7 @@ static void emit_region(std::ostringstream& ss, const Plan& p, Region& r) {
     int vec = 4;
     if (inner.size % 4 != 0) vec = 1;
     for (size_t e = 0; e < next && vec == 4; ++e) {
-        if (r.ext_access[e].imm) continue;
+        if (r.ext_access[e].imm || r.ext_access[e].role != 0) continue;
         int64_t si = inner.st[e];
         if (si != 0 && si != 1) vec = 1;
         if (si == 1) {
@@ -256,6 +310,7 @@ static void emit_region(std::ostringstream& ss, const Plan& p, Region& r) {
         if (r.ext_access[e].imm) continue;
         int64_t o = r.ext_access[e].offset;
         for (const Dim& d : dims) o += (d.size - 1) * d.st[e];
+        if (r.ext_access[e].kcount > 0) o += (r.ext_access[e].kcount - 1) * r.ext_access[e].kstride;
         maxoff = std::max(maxoff, o + 1);
     }
     const char* it = (maxoff < (1LL << 31) - 1024 && nvec * vec < (1LL << 31) - 1024) ? "int" : "long long";
@@ -278,9 +333,20 @@ static void emit_region(std::ostringstream& ss, const Plan& p, Region& r) {
         if (d == 0) ss << "    const I c0 = t;\n";
         else ss << "    const I c" << d << " = t % " << dims[d].size << "; t /= " << dims[d].size << ";\n";
     }
-    // loads
+    // loads (small-K matmul operands are read where the product is formed)
+    std::vector<std::string> offs(next);
     for (size_t e = 0; e < next; ++e) {
         const Access& a = r.ext_access[e];
+        if (a.imm) continue;
+        std::ostringstream off;
+        off << a.offset;
+        for (size_t d = 0; d < dims.size(); ++d)
+            if (dims[d].st[e] != 0) off << " + c" << d << " * (I)" << dims[d].st[e];
+        offs[e] = off.str();
+    }
+    for (size_t e = 0; e < next; ++e) {
+        const Access& a = r.ext_access[e];
+        if (a.role != 0) continue;
         if (a.imm) {
             ss << "    const float a" << e << " = " << flit(a.value) << ";\n";
             continue;
@@ -306,19 +372,36 @@ static void emit_region(std::ostringstream& ss, const Plan& p, Region& r) {
     }
     // compute
     auto ref = [&](int node) -> std::string {
-        auto itx = std::find(r.ext.begin(), r.ext.end(), node);
-        if (itx != r.ext.end()) {
-            size_t e = static_cast<size_t>(itx - r.ext.begin());
+        for (size_t e = 0; e < next; ++e) {
+            if (r.ext[e] != node || r.ext_access[e].role != 0) continue;
             const Access& a = r.ext_access[e];
             bool lane = vec == 4 && !a.imm && inner.st[e] != 0;
             return "a" + std::to_string(e) + (lane ? "[l]" : "");
         }
         return "v" + std::to_string(node);
     };
+    // small-K matmul: A's K values of this element's row (shared by the vector's lanes)
+    for (int i : r.nodes) {
+        if (!g.nodes[static_cast<size_t>(i)].inline_mm) continue;
+        const size_t ea = mm_operand(r, i, 1);
+        const Access& a = r.ext_access[ea];
+        ss << "    float am" << i << "[" << a.kcount << "];\n";
+        ss << "#pragma unroll\n    for (int k = 0; k < " << a.kcount << "; ++k) am" << i << "[k] = __ldg(x" << ea << " + ("
+           << offs[ea] << " + (I)k * " << a.kstride << "));\n";
+    }
     for (size_t s = 0; s < nsto; ++s) ss << "    float o" << s << "[" << vec << "];\n";
     ss << "#pragma unroll\n    for (int l = 0; l < " << vec << "; ++l) {\n";
     for (int i : r.nodes) {
         const Node& nd = g.nodes[static_cast<size_t>(i)];
+        if (nd.inline_mm) {  // one sequential fmaf chain over k, as the small-K GEMM kernel computes it
+            const size_t eb = mm_operand(r, i, 2);
+            const Access& b = r.ext_access[eb];
+            ss << "      float v" << i << " = 0.0f;\n";
+            ss << "#pragma unroll\n      for (int k = 0; k < " << b.kcount << "; ++k) v" << i << " = fmaf(am" << i
+               << "[k], __ldg(x" << eb << " + (" << offs[eb] << " + (I)l * " << inner.st[eb] << " + (I)k * "
+               << b.kstride << ")), v" << i << ");\n";
+            continue;
+        }
         std::string x = ref(nd.in[0]);
         std::string y = nd.in.size() > 1 ? ref(nd.in[1]) : "";
         ss << "      const float v" << i << " = " << node_expr(nd, x, y) << ";\n";

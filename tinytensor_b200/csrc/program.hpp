@@ -109,6 +109,11 @@ struct Access {
     int node = -1;                      // graph node whose storage is read
     int64_t offset = 0;                 // element offset into that storage
     std::vector<int64_t> strides;       // element strides per dim of the READ shape
+    // Operand of a small-K matmul evaluated in the region (node `mm`): role 1 = A (varies
+    // with the row, strides {row, 0}), role 2 = B (varies with the column, {0, column});
+    // the K index steps by kstride, kcount values.  role 0: a plain elementwise read.
+    int role = 0, mm = -1;
+    int64_t kstride = 0, kcount = 0;
 };
 
 struct Region {

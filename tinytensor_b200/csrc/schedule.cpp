@@ -100,6 +100,44 @@ void fold_gemm_epilogues(Graph& g, const std::vector<int>& out_pos) {
     }
 }
 
+// Small-K matmuls evaluated inside their readers' fused region.  A 2-D matmul with
+// K <= 16 (a product bound by writing C) whose readers are all elementwise nodes of its
+// shape is computed where those readers run: each element is a K-term fmaf chain over a
+// row of A and a column of B read from their buffers, so the product is never stored and
+// read back.  The operands must be addressable buffers: not a value of the product's own
+// shape computed in a region (it could live in registers of the same region), not a
+// scalar constant, not another inlined product.
+void mark_inline_matmuls(Graph& g, const std::vector<int>& out_pos) {
+    const size_t n = g.nodes.size();
+    std::vector<std::vector<int>> readers(n);
+    for (size_t i = 0; i < n; ++i)
+        for (int q : g.nodes[i].in) readers[static_cast<size_t>(q)].push_back(static_cast<int>(i));
+    auto base_of = [&](int q) {
+        while (is_view(g.nodes[static_cast<size_t>(q)].op)) q = g.nodes[static_cast<size_t>(q)].in[0];
+        return q;
+    };
+    for (size_t m = 0; m < n; ++m) {
+        Node& mm = g.nodes[m];
+        if (mm.op != TT_OP_MATMUL || mm.epilogue != 0 || out_pos[m] >= 0 || mm.shape.size() != 2) continue;
+        const Shape& sa = g.nodes[static_cast<size_t>(mm.in[0])].shape;
+        const Shape& sb = g.nodes[static_cast<size_t>(mm.in[1])].shape;
+        if (sa.size() != 2 || sb.size() != 2 || mm.shape[0] < 2 || mm.shape[1] < 2) continue;
+        if (sa[1] < 1 || sa[1] > 16 || readers[m].empty()) continue;
+        bool ok = true;
+        for (int u : readers[m]) {
+            const Node& un = g.nodes[static_cast<size_t>(u)];
+            ok &= is_elementwise(un.op) && un.fused_into < 0 && un.shape == mm.shape;
+        }
+        for (int k = 0; k < 2 && ok; ++k) {
+            const Node& b = g.nodes[static_cast<size_t>(base_of(mm.in[static_cast<size_t>(k)]))];
+            if (is_elementwise(b.op) && b.shape == mm.shape) ok = false;
+            if (b.op == TT_OP_CONSTANT && b.cdata.size() <= 1) ok = false;
+            if (b.op == TT_OP_MATMUL && b.inline_mm) ok = false;
+        }
+        mm.inline_mm = ok;
+    }
+}
+
 }  // namespace
 
 int64_t split_copies_bytes(int64_t R, int64_t C, bool rows, bool t) {
@@ -121,6 +159,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
     std::vector<int> out_pos(N0, -1);
     for (size_t k = 0; k < g.outputs.size(); ++k) out_pos[static_cast<size_t>(g.outputs[k])] = static_cast<int>(k);
     if (opt.gemm_epilogue) fold_gemm_epilogues(g, out_pos);
+    if (opt.gemm_epilogue && opt.fuse) mark_inline_matmuls(g, out_pos);
     std::vector<std::vector<int>> users(N0);
     for (size_t i = 0; i < N0; ++i)
         for (int q : g.nodes[i].in) users[static_cast<size_t>(q)].push_back(static_cast<int>(i));
@@ -137,7 +176,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         }
         if (n.dtype != TT_FLOAT32) fail(TT_ERR_COMPILE, "The CUDA backend computes in float32 only (node %" +
                                                             std::to_string(n.id) + " is float64)");
-        if (is_elementwise(n.op) && n.fused_into < 0) {
+        if ((is_elementwise(n.op) && n.fused_into < 0) || n.inline_mm) {
             int R = -1;
             if (opt.fuse) {
                 for (int q : n.in) {
@@ -251,7 +290,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
     // ---- 2. storage ----
     std::vector<bool> stored(N0, false);
     for (size_t i = 0; i < N0; ++i) {
-        if (!is_elementwise(g.nodes[i].op) || g.nodes[i].fused_into >= 0) continue;
+        if ((!is_elementwise(g.nodes[i].op) && !g.nodes[i].inline_mm) || g.nodes[i].fused_into >= 0) continue;
         bool s = out_pos[i] >= 0;
         for (int u : users[i]) s |= p.region_of[static_cast<size_t>(u)] != p.region_of[i];
         stored[i] = s;
@@ -279,6 +318,11 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         const Node& n = g.nodes[i];
         if (n.fused_into >= 0) {  // computed by the matmul's epilogue: a view of its storage
             p.st[i] = p.st[static_cast<size_t>(n.fused_into)];
+            continue;
+        }
+        if (n.inline_mm) {  // computed in its region like an elementwise node
+            if (stored[i]) p.st[i] = make_root(i);
+            else p.st[i].kind = SK_REG;
             continue;
         }
         switch (n.op) {
@@ -342,9 +386,31 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         Region& r = p.regions[R];
         if (r.is_copy) continue;
         for (int i : r.nodes) {
-            for (int q : g.nodes[static_cast<size_t>(i)].in) {
+            const Node& nd = g.nodes[static_cast<size_t>(i)];
+            if (nd.inline_mm) {  // operands: A varies with the row, B with the column, both along K
+                for (int k = 0; k < 2; ++k) {
+                    const int q = nd.in[static_cast<size_t>(k)];
+                    const Storage& sq = p.st[static_cast<size_t>(q)];
+                    if (sq.kind != SK_BUF) fail(TT_ERR_COMPILE, "internal: small-K matmul operand is not a buffer");
+                    Access a;
+                    a.node = sq.root;
+                    a.offset = sq.offset;
+                    a.role = k + 1;
+                    a.mm = i;
+                    a.strides = k == 0 ? std::vector<int64_t>{sq.strides[0], 0} : std::vector<int64_t>{0, sq.strides[1]};
+                    a.kstride = k == 0 ? sq.strides[1] : sq.strides[0];
+                    a.kcount = g.nodes[static_cast<size_t>(q)].shape[k == 0 ? 1 : 0];
+                    r.ext.push_back(q);
+                    r.ext_access.push_back(a);
+                }
+                if (stored[static_cast<size_t>(i)]) r.stores.push_back(i);
+                continue;
+            }
+            for (int q : nd.in) {
                 if (p.region_of[static_cast<size_t>(q)] == static_cast<int>(R)) continue;
-                if (std::find(r.ext.begin(), r.ext.end(), q) != r.ext.end()) continue;
+                bool have = false;
+                for (size_t e = 0; e < r.ext.size(); ++e) have |= r.ext[e] == q && r.ext_access[e].role == 0;
+                if (have) continue;
                 const Storage& sq = p.st[static_cast<size_t>(q)];
                 if (sq.kind == SK_REG) fail(TT_ERR_COMPILE, "internal: region reads an unstored value");
                 r.ext.push_back(q);
@@ -443,7 +509,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
     g.nodes.reserve(N0 * 3 + 8);      // materialise() appends nodes: no reference is held across it
     for (size_t i = 0; i < N0; ++i) {
         const int op = g.nodes[i].op;
-        if (op == TT_OP_MATMUL) {
+        if (op == TT_OP_MATMUL && !g.nodes[i].inline_mm) {
             for (size_t k = 0; k < 2; ++k) {
                 const int src = g.nodes[i].in[k];
                 if (!batch_linear(src, g.nodes[i].shape)) {

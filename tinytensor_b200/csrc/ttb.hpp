@@ -37,6 +37,9 @@ struct Node {
     // and on that activation node the index of the matmul that computes it.
     int epilogue = 0;
     int fused_into = -1;
+    // Set by the scheduler only: a matmul with K <= 16 evaluated inside the fused region
+    // of its elementwise readers (no GEMM launch, no stored product).
+    bool inline_mm = false;
 };
 
 struct Graph {
