@@ -123,7 +123,9 @@ typedef struct tt_compile_options {
 } tt_compile_options;
 
 #define TT_FLAG_NO_FUSION 1       /* one kernel per elementwise node (diagnostics) */
-#define TT_FLAG_NO_GEMM_FUSION 2  /* keep GEMM epilogues plain (diagnostics) */
+#define TT_FLAG_NO_GEMM_FUSION 2  /* no GEMM-adjacent fusion (diagnostics): activations stay separate
+                                   * passes, every tensor-core GEMM splits its own operands, small-K
+                                   * products are GEMM launches */
 #define TT_FLAG_HOST_ONLY 4       /* plan + generate + NVRTC-compile only: no device, no arena
                                      (tt_program_info works; tt_program_run reports no device) */
 #define TT_FLAG_SERIAL 8          /* every launch on the run's stream, one after another (by

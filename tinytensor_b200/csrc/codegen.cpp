@@ -159,7 +159,9 @@ static void emit_region_tiled(std::ostringstream& ss, const Plan& p, Region& r) 
         const Access& b = r.ext_access[eb];
         const int64_t K = a.kcount;
         ss << "  __shared__ float sa" << i << "[32][" << K << "];\n";
-        ss << "  __shared__ __align__(16) float sb" << i << "[" << K << "][128];\n";
+        // pitch 132: the staging stores (consecutive k in consecutive lanes) spread over 8 bank
+        // groups, and each row stays 16-B aligned for the float4 column reads
+        ss << "  __shared__ __align__(16) float sb" << i << "[" << K << "][132];\n";
         ss << "  for (int e = threadIdx.x; e < " << 32 * K << "; e += 256) {\n";
         if (a.kstride == 1) ss << "    const int q = e / " << K << ", k = e % " << K << ";\n";
         else ss << "    const int k = e / 32, q = e % 32;\n";
