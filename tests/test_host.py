@@ -371,3 +371,19 @@ def test_dz_regions_write_the_gemm_operand_copies(cache_dir):
     plain = tt.compile_gradients(g, loss, [w1, w2, w3], cache_dir=cache_dir,
                                  flags=HOST | tt.FLAG_NO_GEMM_FUSION).execution_plan()
     assert "hi/lo" not in plain
+
+
+def test_small_k_product_is_formed_inside_its_region(cache_dir):
+    """The MLP's dH2 = dY W3^T (K = 10, read only by the dZ2 region) is no GEMM launch:
+    the dZ2 region forms it; a small-K product that is also a graph output stays a GEMM."""
+    g = tt.Graph()
+    x, t = g.input([4096, 1024]), g.input([4096, 10])
+    w1, w2, w3 = g.input([1024, 4096]), g.input([4096, 4096]), g.input([4096, 10])
+    d = tt.tanh(tt.relu(x @ w1) @ w2) @ w3 - t
+    loss = tt.mean(d * d)
+    plan = tt.compile_gradients(g, loss, [w1, w2, w3], cache_dir=cache_dir, flags=HOST).execution_plan()
+    assert "simt_smallk" not in plan and "fused[matmul,mul,sub,mul]" in plan, plan
+    g2 = tt.Graph()
+    a, b = g2.input([300, 8]), g2.input([8, 256])
+    m = a @ b
+    assert "simt_smallk" in _host_compile(g2, [m, m * 3.0], cache_dir).execution_plan()
