@@ -142,3 +142,23 @@ def test_region_with_two_stores_copies_one(cache_dir):
     ur = O.binary(O.MUL, a, b)
     assert_bitexact(gu, ur)
     assert_norm(gv, O.matmul(O.binary(O.ADD, ur, a), y), GEMM_FROB_RTOL)
+
+
+@pytest.mark.parametrize("form", ["X Xt", "Xt X"])
+def test_gram_matrix_reads_both_operands_from_one_set_of_copies(form, cache_dir):
+    """X X^T (both operands along X's rows) and X^T X (both across): the GEMM takes A and
+    B from the same region-written copies and runs no pre-pass at all."""
+    rng = np.random.default_rng(59 + len(form))
+    a, b = _data(rng, (512, 384), 1.0), _data(rng, (512, 384), 1.0)
+    g = tt.Graph()
+    na, nb = g.input([512, 384]), g.input([512, 384])
+    x = na * nb
+    out = x @ tt.transpose(x, 0, 1) if form == "X Xt" else tt.transpose(x, 0, 1) @ x
+    prog = tt.compile(g, outputs=[out], cache_dir=cache_dir)
+    plan = prog.execution_plan()
+    assert "(A hi/lo from [0]) (B hi/lo from [0])" in plan, plan
+    got = prog.run({na: a, nb: b}).numpy()
+    xr = O.binary(O.MUL, a, b)
+    xt = np.ascontiguousarray(xr.T)
+    ref = O.matmul(xr, xt) if form == "X Xt" else O.matmul(xt, xr)
+    assert_norm(got, ref, GEMM_FROB_RTOL)
