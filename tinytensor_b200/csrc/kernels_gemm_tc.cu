@@ -776,52 +776,61 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
     }
 }
 
-// M/N-contiguous view (s_r == 1) -> K-major hi/lo[b*l_b + r*l_r + k], transposed in
-// registers: a thread loads a 4 (K) x 4 (rows) block as four float4s along the rows,
-// transposes it in registers and stores four float4s along K for hi and for lo.  A warp
-// covers 32 K x 16 rows (lane = 8 K-quads x 4 row-quads): loads are 64-B runs of 8 K-rows,
-// stores 128-B runs of 4 rows; no shared memory and no barriers.  vec4 (R % 4 == 0, X,
-// s_k and s_b 16-B aligned) allows the float4 loads; K-major rows are padded to
-// l_r >= round4(K), so a store may run into the padding (never read) but not past it.
+// M/N-contiguous view (s_r == 1) -> K-major hi/lo[b*l_b + r*l_r + k]: the source is
+// read as a row-major [K][R] matrix (row stride s_k) in tiles of 32 K-rows x 128 R-columns,
+// one CTA per tile.  Each warp loads rows w, w+8, w+16, w+24 of the tile with a float4 of
+// columns per lane (all four loads issued before the tile is parked in shared memory,
+// pitch 132 floats: float4 stores and float4 column-chunk reads at the minimum four
+// wavefronts); then lane = K offset, and each warp splits and writes 16 of the tile's
+// columns as 128-B runs of hi and lo along K.  Tiles are numbered K first, so the CTAs
+// resident together extend the same hi/lo rows.  vec4 (R % 4 == 0, X, s_k and s_b
+// 16-B aligned) allows the float4 loads.  Only k < K is written (the rows' padding up to
+// l_r is never read).
 __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ X, float* __restrict__ hi,
                                                               float* __restrict__ lo, int64_t R, int64_t K,
                                                               int64_t s_k, int64_t s_b, int64_t l_r, int64_t l_b,
                                                               int vec4) {
+    __shared__ __align__(16) float tile[32][132];
     const int64_t b = blockIdx.y;
-    const int lane = threadIdx.x & 31;
-    const int q = lane & 7, c = lane >> 3;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t tiles_k = (K + 31) / 32;
+    const int64_t k0 = (static_cast<int64_t>(blockIdx.x) % tiles_k) * 32;
+    const int64_t r0 = (static_cast<int64_t>(blockIdx.x) / tiles_k) * 128;
     const float* xb = X + b * s_b;
+    const int64_t r = r0 + 4 * lane;
+    float4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t k = k0 + w + 8 * i;
+        const float* src = xb + k * s_k + r;
+        if (vec4 && k < K && r < R) {
+            v[i] = __ldg(reinterpret_cast<const float4*>(src));
+        } else {
+            v[i].x = (k < K && r < R) ? __ldg(src) : 0.0f;
+            v[i].y = (k < K && r + 1 < R) ? __ldg(src + 1) : 0.0f;
+            v[i].z = (k < K && r + 2 < R) ? __ldg(src + 2) : 0.0f;
+            v[i].w = (k < K && r + 3 < R) ? __ldg(src + 3) : 0.0f;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) *reinterpret_cast<float4*>(&tile[w + 8 * i][4 * lane]) = v[i];
+    __syncthreads();
+    const int64_t k = k0 + lane;
     float* hb = hi + b * l_b;
     float* lb = lo + b * l_b;
-    const int64_t tk_n = (K + 31) / 32, tiles = tk_n * ((R + 15) / 16);
-    const int64_t warps = static_cast<int64_t>(gridDim.x) * 8;
-    for (int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); t < tiles; t += warps) {
-        const int64_t tr = t / tk_n;
-        const int64_t k = (t - tr * tk_n) * 32 + 4 * q;   // this thread's 4 K values k..k+3
-        const int64_t r = tr * 16 + 4 * c;                 // and 4 rows r..r+3
-        float v[4][4];                                     // v[j][i] = X[k+j][r+i]
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float* src = xb + (k + j) * s_k + r;
-            if (vec4 && k + j < K && r < R) {
-                const float4 x = __ldg(reinterpret_cast<const float4*>(src));
-                v[j][0] = x.x; v[j][1] = x.y; v[j][2] = x.z; v[j][3] = x.w;
-            } else {
+    for (int j = 0; j < 4; ++j) {
+        const float4 q = *reinterpret_cast<const float4*>(&tile[lane][w * 16 + 4 * j]);
+        const float qv[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i) v[j][i] = (k + j < K && r + i < R) ? __ldg(src + i) : 0.0f;
+        for (int u = 0; u < 4; ++u) {
+            const int64_t rr = r0 + w * 16 + 4 * j + u;
+            if (rr < R && k < K) {
+                float h, l;
+                split_tf32(qv[u], h, l);
+                hb[rr * l_r + k] = h;
+                lb[rr * l_r + k] = l;
             }
-        }
-        if (k >= l_r) continue;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            if (r + i >= R) break;
-            float4 h, l;
-            split_tf32(v[0][i], h.x, l.x);
-            split_tf32(v[1][i], h.y, l.y);
-            split_tf32(v[2][i], h.z, l.z);
-            split_tf32(v[3][i], h.w, l.w);
-            *reinterpret_cast<float4*>(hb + (r + i) * l_r + k) = h;
-            *reinterpret_cast<float4*>(lb + (r + i) * l_r + k) = l;
         }
     }
 }
@@ -850,15 +859,9 @@ int launch_split(const float* X, float* hi, float* lo, int64_t R, int64_t K, int
     const bool x16 = (reinterpret_cast<uintptr_t>(X) & 15) == 0 && (o.nb == 1 || s_b % 4 == 0);
     if (s_r == 1 && s_k != 1 && R > 1 && K > 1) {
         const bool vec4 = x16 && R % 4 == 0 && s_k % 4 == 0;
-        // one resident wave of grid-stride CTAs (8 warps each, a 32 x 16 tile per warp)
-        static const int per_sm = [] {
-            int n = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, split_transpose_kernel, 256, 0) != cudaSuccess) n = 4;
-            return n > 0 ? n : 1;
-        }();
-        int64_t blocks = (((R + 15) / 16) * ((K + 31) / 32) + 7) / 8;
-        if (blocks > 148 * per_sm) blocks = 148 * per_sm;
-        split_transpose_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(o.nb)), 256, 0, st>>>(
+        const int64_t tiles = ((K + 31) / 32) * ((R + 127) / 128);  // one CTA per 32 (K) x 128 (R) tile
+        if (tiles > 0x7FFFFFFFLL) return static_cast<int>(cudaErrorInvalidValue);
+        split_transpose_kernel<<<dim3(static_cast<unsigned>(tiles), static_cast<unsigned>(o.nb)), 256, 0, st>>>(
             X, hi, lo, R, K, s_k, s_b, o.lr, o.lb, vec4 ? 1 : 0);
         return static_cast<int>(cudaGetLastError());
     }
