@@ -18,6 +18,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -93,7 +94,9 @@ class ClockSampler:
     def __init__(self, device):
         self.device = device
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+        # raw samples: TT_BENCH_CLOCKS_DIR if set, else the system temp directory
+        out_dir = os.environ.get("TT_BENCH_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(out_dir, f"clocks_bench_{os.getpid()}.csv")
 
     def start(self):
         try:
