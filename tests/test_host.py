@@ -387,3 +387,46 @@ def test_small_k_product_is_formed_inside_its_region(cache_dir):
     a, b = g2.input([300, 8]), g2.input([8, 256])
     m = a @ b
     assert "simt_smallk" in _host_compile(g2, [m, m * 3.0], cache_dir).execution_plan()
+
+
+def _region_variant_graphs():
+    """Graphs whose regions use every generated-kernel variant of the GEMM-adjacent
+    fusion: tiled regions writing one or both copy layouts (with and without the fp32
+    store, odd sizes, broadcast operands) and small-K products in flat and tiled regions."""
+    out = []
+    for r, c, use in [(1024, 512, "A=Xt"), (646, 258, "B=X"), (646, 258, "A=X"), (100, 1030, "A=Xt")]:
+        g = tt.Graph()
+        a, b = g.input([r, c]), g.input([r, c])
+        x = a * b
+        k = c if use == "A=X" else r
+        y = g.input([k, 64] if use.startswith("A") else [64, k])
+        o = {"A=X": lambda: x @ y, "A=Xt": lambda: tt.transpose(x, 0, 1) @ y, "B=X": lambda: y @ x}[use]()
+        out.append((g, [o]))
+    for bshape in [(1, 520), (300, 1)]:
+        g = tt.Graph()
+        a, b, y = g.input([300, 520]), g.input(list(bshape)), g.input([300, 96])
+        out.append((g, [tt.transpose(tt.relu(a + b) * 0.5, 0, 1) @ y]))
+    g = tt.Graph()
+    a, b, y1, y2 = g.input([768, 512]), g.input([768, 512]), g.input([512, 192]), g.input([768, 160])
+    x = tt.relu(a - b)
+    out.append((g, [x, x @ y1, tt.transpose(x, 0, 1) @ y2]))
+    g = tt.Graph()
+    a, b, c = g.input([300, 10]), g.input([10, 522]), g.input([300, 522])
+    out.append((g, [(a @ b) * c]))  # flat region, scalar lanes (522 % 4 != 0)
+    g = tt.Graph()
+    t, w, yy, h, v = g.input([1024, 10]), g.input([512, 10]), g.input([1024, 512]), g.input([1024, 384]), g.input([512, 256])
+    dz = (tt.relu(t) @ tt.transpose(w, 0, 1)) * (1.0 - yy * yy)
+    out.append((g, [tt.transpose(h, 0, 1) @ dz, dz @ v]))
+    return out
+
+
+def test_gemm_adjacent_region_variants_compile(cache_dir):
+    """NVRTC compiles every variant (host-only: plan + generate + compile to sm_100a)."""
+    seen = set()
+    for g, outs in _region_variant_graphs():
+        p = _host_compile(g, outs, cache_dir)
+        plan, src = p.execution_plan(), p.generated_source()
+        assert "Binary Object:" in plan
+        seen.update(k for k in ("tiled", "(writes hi/lo of X^T", "(writes hi/lo of X,", "hi/lo of X and X^T)",
+                                "fused[matmul,") if k in src or k in plan)
+    assert len(seen) == 5, seen
