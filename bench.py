@@ -11,6 +11,8 @@ At N=1 the line also carries the single-GPU components of the metric (fused
 elementwise GB/s, reductions GB/s, fp32-accurate GEMM TFLOP/s).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py --batch 8192 ...          # a smaller MLP step (profiling case)
+    python bench.py --workload gemm --size M,N,K ...   # one compiled program (profiling case)
 """
 
 import argparse
