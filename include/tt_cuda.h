@@ -241,10 +241,14 @@ int tt_sgd_step(int32_t n, float* const* params, const float* const* grads, floa
  * call cudaMalloc: its scratch is a static device array of 32 MiB per GPU that loads
  * the library (held until exit); products needing more are rejected with
  * TT_ERR_MEMORY.  The first call on a device resolves the array's address
- * (cudaGetSymbolAddress) and should come before any stream capture.  All calls share
- * the array: calls that overlap on the GPU race, so order them on one stream.
- * device_status: optional device int the kernels set if a bounded wait gives up
- * (caller clears it); NULL uses an internal word. */
+ * (cudaGetSymbolAddress); under lazy module loading that also loads the module and
+ * reserves the array, and the kernels load on their first launch, so make the first
+ * call on each device a warm-up outside any no-allocation window and before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU race, so
+ * order them on one stream.  A, B may be NULL when they hold no elements (K = 0).
+ * device_status: optional zeroed device int that the kernels set if a bounded wait
+ * gives up; check it after synchronising.  With NULL an internal word takes the code
+ * and such a timeout is NOT reported (the call still returns TT_OK, C partly written). */
 int tt_gemm_f32_noalloc(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
                         int32_t* device_status, void* stream);
 

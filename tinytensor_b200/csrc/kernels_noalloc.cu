@@ -11,12 +11,20 @@
 //  - scratch capacity TT_NOALLOC_SCRATCH_BYTES (32 MiB); products whose plan needs more
 //    are rejected with TT_ERR_MEMORY and a message naming the need and the capacity;
 //  - the first call on a device looks up the array's device address with
-//    cudaGetSymbolAddress (with that device current); make that first call before any
-//    stream capture;
+//    cudaGetSymbolAddress (with that device current).  Under lazy module loading that
+//    lookup is also what loads this module and reserves the array, and the GEMM kernels
+//    load on their first launch, so the first call on each device can itself need
+//    device memory: make it once as a warm-up, outside any no-allocation window and
+//    before any stream capture.  The address is cached only once a lookup succeeds, so a
+//    failed first attempt can be retried;
 //  - every call shares the one array, which keeps the previous call's contents.  All
 //    of it is rewritten before it is read, except the status word, which each call
 //    clears on its stream.  Calls whose work overlaps on the GPU (other streams, or
-//    other host threads) race on the array: order them on one stream.
+//    other host threads) race on the array: order them on one stream;
+//  - device_status NULL: a bounded wait that gives up inside the tensor-core kernels
+//    records its code in an internal word that nothing reports, so the call still
+//    returns TT_OK with C partly written.  Callers that need to detect that pass their
+//    own zeroed device int and check it after synchronising the stream.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -33,27 +41,43 @@ namespace {
 static __device__ __align__(256) unsigned char g_noalloc_scratch[TT_NOALLOC_SCRATCH_BYTES + TT_NOALLOC_STATUS_BYTES];
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_once[kMaxDevices];
-void* g_addr[kMaxDevices];
-cudaError_t g_setup_err[kMaxDevices];
+std::mutex g_mu;
+void* g_addr[kMaxDevices];  // non-null once a lookup on that device succeeded
+
+// Device address of the scratch array on the current device `dev` (looked up once).
+cudaError_t scratch_address(int dev, void** out) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_addr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();
+            return e != cudaSuccess ? e : cudaErrorInvalidSymbol;
+        }
+        g_addr[dev] = p;
+    }
+    *out = g_addr[dev];
+    return cudaSuccess;
+}
 
 }  // namespace
 
 extern "C" int tt_gemm_f32_noalloc(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
                                    int32_t* device_status, void* stream) {
     using namespace ttb;
-    if (!A || !B || !C || M < 0 || N < 0 || K < 0) return record_error(TT_ERR_INVALID, "bad GEMM arguments");
+    if (M < 0 || N < 0 || K < 0) return record_error(TT_ERR_INVALID, "tt_gemm_f32_noalloc: negative dimension");
+    // Operands are only dereferenced when they hold elements.
+    if ((M > 0 && N > 0 && !C) || (M > 0 && K > 0 && !A) || (K > 0 && N > 0 && !B))
+        return record_error(TT_ERR_INVALID, "tt_gemm_f32_noalloc: null pointer for a non-empty operand");
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
         cudaGetLastError();
         return record_error(TT_ERR_NO_DEVICE, "no current CUDA device");
     }
-    std::call_once(g_once[dev], [dev] {
-        g_setup_err[dev] = cudaGetSymbolAddress(&g_addr[dev], g_noalloc_scratch);
-    });
-    if (g_setup_err[dev] != cudaSuccess || !g_addr[dev])
-        return record_error(TT_ERR_RUNTIME, std::string("cudaGetSymbolAddress(scratch): ") +
-                                                cudaGetErrorString(g_setup_err[dev]));
+    void* addr = nullptr;
+    const cudaError_t se = scratch_address(dev, &addr);
+    if (se != cudaSuccess)
+        return record_error(TT_ERR_RUNTIME, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(se));
     if (M == 0 || N == 0) return TT_OK;
 
     GemmDesc d;
@@ -72,7 +96,7 @@ extern "C" int tt_gemm_f32_noalloc(const float* A, const float* B, float* C, int
                                                "x" + std::to_string(K) + " product needs " + std::to_string(need) +
                                                " bytes of scratch; the static capacity is " +
                                                std::to_string(TT_NOALLOC_SCRATCH_BYTES));
-    char* base = static_cast<char*>(g_addr[dev]);
+    char* base = static_cast<char*>(addr);
     int* status = device_status ? device_status : reinterpret_cast<int*>(base + TT_NOALLOC_SCRATCH_BYTES);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (!device_status) {
