@@ -137,9 +137,38 @@ def test_config4_mlp_gradients_small_batch(cache_dir):
         assert_norm(got, r, GEMM_FROB_RTOL)
 
 
-def test_config4_mlp_full_batch_runs(cache_dir):
-    """Batch 4096: loss matches the oracle forward; gradients are finite and W3's
-    gradient matches an fp64 recomputation from the GPU's own activations' inputs."""
+def _fp64_mlp(x, t, w, cols):
+    """fp64 forward and backward of the MLP (the VJPs of src/autodiff/gradient.cpp:
+    relu mask g * (z > 0), tanh' = 1 - y^2, matmul g.B^T and A^T.g, mean = sum / n).
+    Returns the loss, dW3 in full, and columns `cols` of dW2 and dW1.  Runs in torch
+    float64 on the GPU (cuBLAS DGEMM), an independent fp64 computation."""
+    import torch
+
+    dev = torch.device("cuda")
+    X = torch.from_numpy(x).to(dev, torch.float64)
+    T = torch.from_numpy(t).to(dev, torch.float64)
+    W1, W2, W3 = (torch.from_numpy(a).to(dev, torch.float64) for a in w)
+    c = torch.from_numpy(np.asarray(cols, np.int64)).to(dev)
+    z1 = X @ W1
+    h1 = torch.clamp_min(z1, 0.0)
+    h2 = torch.tanh(h1 @ W2)
+    d = h2 @ W3 - T
+    loss = torch.mean(d * d)
+    dy = 2.0 * d / d.numel()
+    dz2 = (dy @ W3.T) * (1.0 - h2 * h2)
+    gw3 = h2.T @ dy
+    gw2 = h1.T @ dz2[:, c]
+    dz1c = (dz2 @ W2[c, :].T) * (z1[:, c] > 0).to(torch.float64)
+    gw1 = X.T @ dz1c
+    out = (float(loss), gw3.cpu().numpy(), gw2.cpu().numpy(), gw1.cpu().numpy())
+    del X, T, W1, W2, W3, z1, h1, h2, d, dy, dz2
+    torch.cuda.empty_cache()
+    return out
+
+
+def test_config4_mlp_full_batch_gradients(cache_dir):
+    """Batch 4096 (the config's size): loss, dW3 in full and sampled columns of dW2 and
+    dW1 against an fp64 recomputation, relative Frobenius <= 1e-5."""
     B = 4096
     rng = np.random.default_rng(3)
     g, (X, T, W1, W2, W3), loss = _mlp_graph(B)
@@ -148,12 +177,45 @@ def test_config4_mlp_full_batch_runs(cache_dir):
     prog = tt.compile_gradients(g, loss, [W1, W2, W3], cache_dir=cache_dir)
     out = [t.numpy() for t in prog.run(feed)]
     assert all(np.all(np.isfinite(o)) for o in out)
-    x64 = feed[X].astype(np.float64)
-    h2 = np.tanh(np.maximum(x64 @ feed[W1], 0) @ feed[W2])
-    d = h2 @ feed[W3] - feed[T]
-    np.testing.assert_allclose(out[0], np.mean(d * d), rtol=1e-5)
-    gw3 = h2.T @ (2.0 * d / d.size)
+    cols = np.unique(np.random.default_rng(21).integers(0, 4096, 96))
+    l64, gw3, gw2, gw1 = _fp64_mlp(feed[X], feed[T], [feed[W1], feed[W2], feed[W3]], cols)
+    np.testing.assert_allclose(out[0], l64, rtol=1e-5)
     assert_norm(out[3], gw3, GEMM_FROB_RTOL)
+    assert_norm(out[2][:, cols], gw2, GEMM_FROB_RTOL)
+    assert_norm(out[1][:, cols], gw1, GEMM_FROB_RTOL)
+
+
+def test_config5_dp_step_full_global_batch_one_gpu(cache_dir):
+    """One DataParallelSGD step at the benchmark's global batch 32768 on one GPU (the
+    program, the single all-reduce-free update with lr 0.01): the gradients it used
+    against fp64 (dW3 in full, sampled columns of dW2 and dW1, relative Frobenius
+    <= 1e-5), the loss, and the updated weights bit-exact against numpy's float32
+    p - lr * g on those gradients (python/tinytensor/optim.py:18-35)."""
+    B = 32768
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((B, 1024)).astype(np.float32)
+    t = rng.standard_normal((B, 10)).astype(np.float32)
+    ws = [_xavier(rng, 1024, 4096), _xavier(rng, 4096, 4096), _xavier(rng, 4096, 10)]
+    g, (X, T, W1, W2, W3), loss = _mlp_graph(B)
+    prog = tt.compile_gradients(g, loss, [W1, W2, W3], cache_dir=cache_dir)
+    dx, dt = tt.DeviceBuffer.from_numpy(x), tt.DeviceBuffer.from_numpy(t)
+    dw = [tt.DeviceBuffer.from_numpy(w) for w in ws]
+    trainer = tt.DataParallelSGD(prog, dw, lr=0.01)
+    st = tt.Stream()
+    trainer.step([dx, dt], st)
+    st.synchronize()
+    assert prog.status() == 0
+    grads = trainer.grads.numpy()
+    offs = np.cumsum([0] + trainer.sizes)
+    gpu_g = [grads[offs[i]:offs[i + 1]].reshape(ws[i].shape) for i in range(3)]
+    cols = np.unique(np.random.default_rng(22).integers(0, 4096, 64))
+    l64, gw3, gw2, gw1 = _fp64_mlp(x, t, ws, cols)
+    np.testing.assert_allclose(trainer.loss.numpy(), l64, rtol=1e-5)
+    assert_norm(gpu_g[2], gw3, GEMM_FROB_RTOL)
+    assert_norm(gpu_g[1][:, cols], gw2, GEMM_FROB_RTOL)
+    assert_norm(gpu_g[0][:, cols], gw1, GEMM_FROB_RTOL)
+    for w0, gg, d in zip(ws, gpu_g, dw):
+        assert_bitexact(d.numpy(), (w0 - np.float32(0.01) * gg).astype(np.float32))
 
 
 def test_config5_sgd_steps_match_oracle(cache_dir):

@@ -120,6 +120,17 @@ def test_reduce_max_nan_propagates():
     assert np.isnan(r[0]) and r[1] == 6
 
 
+def test_reduce_max_signed_zeros_give_plus_zero_in_any_order():
+    """IEEE 754-2019 maximum(): -0 < +0, so a cell holding both zeros is +0 whichever
+    comes first in the walk; a cell of -0 alone stays -0."""
+    x = np.array([[-0.0, 0.0, -0.0], [0.0, -0.0, -0.0], [-0.0, -0.0, -0.0], [-0.0, -0.0, 0.0]], np.float32)
+    r = O.reduce(O.REDUCE_MAX, x, [1])
+    assert r.tolist() == [0.0, 0.0, 0.0, 0.0]
+    assert np.signbit(r).tolist() == [False, False, True, False]
+    c = O.reduce(O.REDUCE_MAX, x, [0])
+    assert np.signbit(c).tolist() == [False, False, False]
+
+
 def test_sgd_matches_numpy_float32():
     rng = np.random.default_rng(0)
     p, g = rng.standard_normal(100).astype(np.float32), rng.standard_normal(100).astype(np.float32)

@@ -3,8 +3,8 @@
 // Semantics restate the reference's eager ops (src/core/operators.cpp:394-516):
 // float32 data accumulated in double, cast to float at the end; mean is
 // float(sum) * float(1/count) in float.  max (no reference op) keeps a float
-// running maximum that propagates NaN, so the result is order independent and
-// bit-exact against the CPU oracle.
+// running maximum with IEEE 754-2019 maximum() semantics (NaN propagates, -0 < +0),
+// so the result is order independent and bit-exact against the CPU oracle.
 //
 // Layouts (views folded by the scheduler, so a transposed input costs nothing):
 //   ROW  out[o] = red_r x[o*s_outer + r]     one warp per (row, split); float4 when possible
@@ -39,7 +39,8 @@ struct Acc<RO_MEAN> : Acc<RO_SUM> {};
 template <>
 struct Acc<RO_MAX> {
     float v = -INFINITY;
-    __device__ void add(float x) { v = (x > v || x != x) ? x : v; }
+    // x wins when larger, when NaN, or when both are zeros and v is -0 (x is then +0 or -0)
+    __device__ void add(float x) { v = (x > v || x != x || (x == v && __float_as_uint(v) == 0x80000000u)) ? x : v; }
     __device__ void merge(double o) { add(static_cast<float>(o)); }
     __device__ double get() const { return static_cast<double>(v); }
 };
@@ -57,7 +58,7 @@ __device__ __forceinline__ double warp_merge(double v) {
         double w = __shfl_xor_sync(0xffffffffu, v, o);
         if (OP == RO_MAX) {
             float a = static_cast<float>(v), b = static_cast<float>(w);
-            v = (b > a || b != b) ? w : v;
+            v = (b > a || b != b || (b == a && __float_as_uint(a) == 0x80000000u)) ? w : v;
         } else {
             v += w;
         }
