@@ -42,18 +42,40 @@ def load_peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
+def launch_key(label):
+    """(kind, MxNxK) of a GEMM launch label such as
+    'gemm/tcgen05_3xtf32[32768x4096x4096 A:K B:N +tanh]', else (label, None)."""
+    if "[" not in label:
+        return label, None
+    kind, rest = label.split("[", 1)
+    return kind, rest.split()[0].rstrip("]")
+
+
 def load_traffic(label):
-    """DRAM bytes per launch measured by ncu for `label` (profiles/traffic_per_launch.txt,
-    lines '<launch label> <bytes> <how>'), or None."""
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum, one ncu
+    capture) for the launch's kind and shape, from profiles/traffic_per_launch.txt
+    (lines '<kind> <MxNxK> <bytes> <how>'), or None when that launch was not captured."""
     p = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
     if not os.path.exists(p):
         return None
+    kind, shape = launch_key(label)
     with open(p) as f:
         for line in f:
             parts = line.strip().split()
-            if len(parts) >= 2 and not line.startswith("#") and label.startswith(parts[0]):
-                return int(float(parts[1]))
+            if len(parts) >= 3 and not line.startswith("#") and parts[0] == kind and parts[1] == shape:
+                return int(float(parts[2]))
     return None
+
+
+def headline_config(batch, world):
+    """The workload's config, identical in both arms."""
+    return {"workload": "mlp_dp_sgd_step", "model": "MLP 1024-4096-4096-10 MSE", "global_batch": batch,
+            "per_gpu_batch": batch // world, "lr": LR, "parallelism": f"dp{world}",
+            "l2": "inputs larger than L2 (activations 512 MiB per 32768 rows, weights 84 MB)",
+            "tflops_per_step": round(mlp_flops(batch) / 1e12, 4)}
+
+
+HEADLINE_METRIC = "MLP DP SGD step/s (1024-4096-4096-10, global batch {})"
 
 
 def mlp_flops(rows, with_dx=False):
@@ -194,7 +216,6 @@ def run_b200(args):
     for _ in range(args.warmup):
         step()
     barrier()
-    prog.set_profiling(True)
     clocks = ClockSampler(local)
     clocks.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -209,6 +230,15 @@ def run_b200(args):
     ms = ev0.elapsed_time(ev1) / args.steps
     clk = clocks.stop()
     ms = max_over_ranks(ms)
+    assert prog.status() == 0
+
+    # per-launch device times: a second pass of the same steps with an event pair around
+    # every launch (kept out of the headline pass above, whose timing it would disturb)
+    prog.set_profiling(True)
+    barrier()
+    for _ in range(args.steps):
+        step()
+    barrier()
     prof = prog.profile()
     prog.set_profiling(False)
     assert prog.status() == 0
@@ -266,14 +296,15 @@ def run_b200(args):
         "burst_peak": round(burst_peak, 1),
         "avg_ms": round(top_ms, 4),
         "timed": "CUDA events on the launch stream around the GEMM launch (its hi/lo split pre-pass and "
-                 "split-K reduce included)",
+                 "split-K reduce included), averaged over a second pass of the same steps run right after the "
+                 "headline pass (the headline pass itself records no per-launch events)",
     }
     total_prof = sum(t for _, t in prof)
     step_profile = [{"launch": lbl, "ms": round(t, 4), "share": round(t / total_prof, 4)}
                     for lbl, t in sorted(prof, key=lambda p: -p[1])[:10]]
     step_flops = mlp_flops(batch)
     out = {
-        "metric": f"MLP DP SGD step/s (1024-4096-4096-10, global batch {batch})",
+        "metric": HEADLINE_METRIC.format(batch),
         "value": round(1000.0 / ms, 4),
         "unit": "step/s",
         "n_gpus": world,
@@ -285,10 +316,7 @@ def run_b200(args):
         "vs_baseline": None,
         "dtype": "f32 (3xTF32 tensor-core GEMM, fp32 accumulate)",
         "data": "synthetic: X,T ~ N(0,1) seed 4; Xavier-uniform weights seed 4",
-        "config": {"workload": "mlp_dp_sgd_step", "model": "MLP 1024-4096-4096-10 MSE", "global_batch": batch,
-                   "per_gpu_batch": rows, "lr": LR, "parallelism": f"dp{world}",
-                   "l2": "inputs larger than L2 (activations 512 MiB at N=1, weights 84 MB)",
-                   "tflops_per_step": round(step_flops / 1e12, 4)},
+        "config": headline_config(batch, world),
         "tflops": round(step_flops / (ms * 1e-3) / 1e12, 2),
         "e2e": {"value": round(1000.0 / e2e_ms, 4), "unit": "step/s",
                 "h2d_bytes_per_step": int(dx.nbytes + dt.nbytes) * world, "d2h_bytes_per_step": 4 * world},
@@ -300,7 +328,7 @@ def run_b200(args):
     if world == 1 and not args.no_components:
         out["components"] = components(tt, torch, args, peaks, peak_src)
     if rank == 0 and not args.no_cpu_baseline and world == 1 and batch == GLOBAL_BATCH:
-        out["cpu_baseline"] = cpu_baseline(args, sample_rows=64)
+        out["cpu_baseline"] = cpu_baseline(batch)
     if dist is not None:
         dist.barrier()
         comm.close()
@@ -423,84 +451,90 @@ def components(tt, torch, args, peaks, peak_src):
 # CPU baseline: the reference itself (oracle/_ref) on the host cores
 # --------------------------------------------------------------------------------------------
 
-def _ref_worker(args):
-    rows, seed = args
-    sys.path.insert(0, ROOT)
-    import tinytensor_b200.graph as tg
-    from oracle import oracle as O
-
-    class _NS:
-        pass
-    ns = _NS()
-    for k in ("Graph", "relu", "tanh", "mean"):
-        setattr(ns, k, getattr(tg, k))
-    g, (X, T, W1, W2, W3), loss = mlp_graph(ns, rows)
-    x, t, w = mlp_data(seed, rows)
-    feed = {X: x, T: t, W1: w[0], W2: w[1], W3: w[2]}
-    ref = O.Reference()
-    g.mark_output(loss)
-    t_fwd = ref.time_runs(g, feed, mode="avx2", reps=1)       # prog.run(feed): compiled forward
-    t_grad = ref.time_gradients(g, loss, feed, reps=1)        # tt.gradients: eager fwd + bwd
-    return t_fwd + t_grad
+def _reference_runner(batch):
+    """The reference's own data-parallel step (oracle/ref_step.py) over all host cores
+    on the headline batch, prepared (graphs built, forward JIT-compiled) outside any
+    timing; (runner, None) or (None, why not)."""
+    from oracle import ref_step
+    if not ref_step.available():
+        return None, "oracle/_ref/libttref.so not built (the reference sources were absent at build time)"
+    x, t, w = mlp_data(rows=batch)
+    return ref_step.ReferenceStep(x, t, w, lr=LR), None
 
 
-def cpu_baseline(args, sample_rows=64):
-    """Reference step time on the host cores: P processes, each timing the reference's
-    own step (compiled AVX2 forward + eager tt.gradients) on a `sample_rows` shard;
-    the SGD update (84 MB of numpy) is not included.  Extrapolated to the 32768-row step."""
-    import multiprocessing as mp
+def _reference_sample(runner, steps, wall_s):
+    return (f"{steps} full {runner.rows}-row step(s) of the reference itself (oracle/_ref: compiled from its "
+            f"sources), each = {runner.P} processes x {runner.rows // runner.P} rows running the compiled AVX2 "
+            f"forward (tt.compile mode avx2, optimize=True) + eager tt.gradients, shard gradients summed and "
+            f"SGD (lr/{runner.P} on the sum) applied in the parent; graph build and g++ JIT excluded; "
+            f"{wall_s:.1f} s timed")
 
-    sys.path.insert(0, ROOT)
-    from oracle import oracle as O
-    if not O.reference_available():
-        return {"value": None, "unit": "step/s", "cores": 0, "kind": "reference",
-                "sample": "oracle/_ref/libttref.so not built"}
-    P = max(1, min(os.cpu_count() or 1, 64))
-    ctx = mp.get_context("spawn")
-    t0 = time.time()
-    with ctx.Pool(P) as pool:
-        times = pool.map(_ref_worker, [(sample_rows, 100 + i) for i in range(P)])
-    wall = time.time() - t0
-    per = float(np.median(times))
-    rows_per_s = P * sample_rows / per
-    return {"value": round(rows_per_s / GLOBAL_BATCH, 6), "unit": "step/s", "cores": P, "kind": "reference",
-            "sample": f"{P} processes x {sample_rows}-row shard of the MLP step (reference AVX2 compiled forward + "
-                      f"eager tt.gradients), median {per:.2f} s per shard, wall {wall:.1f} s; extrapolated to "
-                      f"{GLOBAL_BATCH} rows"}
+
+def cpu_baseline(batch):
+    """One real step of the reference at the headline batch on the host cores (rank 0,
+    N=1): no extrapolation from smaller shards."""
+    runner, why = _reference_runner(batch)
+    if runner is None:
+        return {"value": None, "unit": "step/s", "cores": 0, "kind": "reference", "sample": why}
+    try:
+        s = runner.step()
+        info = {"value": round(1.0 / s, 6), "unit": "step/s", "cores": runner.P, "kind": "reference",
+                "sample": _reference_sample(runner, 1, s), "shard_s_max": round(runner.last["shard_s_max"], 2),
+                "reduce_update_s": round(runner.last["reduce_update_s"], 2)}
+    finally:
+        runner.close()
+    return info
+
+
+# Timed full reference steps stop once this much wall time is spent (at least one step),
+# so `--impl reference` ends within a few minutes whatever --steps asks for; the line
+# reports the steps actually timed.
+REFERENCE_TIME_BUDGET_S = 120.0
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    vals = []
-    info = None
-    for i in range(args.warmup + args.steps):
-        info = cpu_baseline(args, sample_rows=32)
-        if i >= args.warmup and info["value"] is not None:
-            vals.append(info["value"])
-    if not vals:
-        print(json.dumps({"impl": "reference", "unavailable": info["sample"] if info else "no sample"}))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    runner, why = _reference_runner(args.batch)
+    if runner is None:
+        print(json.dumps({"impl": "reference", "unavailable": why}))
         return
-    v = float(np.median(vals))
-    info["value"] = round(v, 6)
+    try:
+        # No untimed full steps: preparing the runner already built the graphs and compiled
+        # the forward, and the reference allocates afresh in every call, so its first step
+        # costs what later ones do (measured: 90 and 95 s for 2048-row shards on 8 cores).
+        warm = 0
+        times = []
+        while len(times) < args.steps and (not times or sum(times) < REFERENCE_TIME_BUDGET_S):
+            times.append(runner.step())
+        last = dict(runner.last)
+        P = runner.P
+        sample = _reference_sample(runner, len(times), sum(times))
+    finally:
+        runner.close()
+    s = float(np.mean(times))
+    v = 1.0 / s
     out = {
         "impl": "reference",
-        "metric": "MLP DP SGD step/s (1024-4096-4096-10, global batch 32768)",
+        "metric": HEADLINE_METRIC.format(args.batch),
         "value": round(v, 6),
         "unit": "step/s",
         "n_gpus": args.gpus,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(1000.0 / v, 1),
+        "steps": len(times),
+        "warmup": warm,
+        "ms_per_step": round(1000.0 * s, 1),
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic: X,T ~ N(0,1); Xavier-uniform weights",
-        "config": {"workload": "mlp_dp_sgd_step", "model": "MLP 1024-4096-4096-10 MSE", "global_batch": GLOBAL_BATCH,
-                   "parallelism": "reference CPU, all host cores"},
-        "cpu_baseline": info,
+        "data": "synthetic: X,T ~ N(0,1) seed 4; Xavier-uniform weights seed 4",
+        "config": headline_config(args.batch, world),
+        "note": (f"the reference is CPU-only: {P} host processes run it; steps/warmup are the full steps actually "
+                 f"run ({REFERENCE_TIME_BUDGET_S:.0f} s budget for timed steps)"),
+        "cpu_baseline": {"value": round(v, 6), "unit": "step/s", "cores": P, "kind": "reference", "sample": sample,
+                         "step_s": [round(t, 2) for t in times], "shard_s_max_last": round(last["shard_s_max"], 2)},
         "e2e": {"value": round(v, 6), "unit": "step/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out))
