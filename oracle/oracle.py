@@ -368,7 +368,8 @@ def gradients(graph, loss, feed, wrt):
 class Reference:
     """The reference TinyTensor library (oracle/_ref/libttref.so)."""
 
-    MODES = {"interpreted": 0, "scalar": 1, "avx2": 2, "avx2_fma": 3, "avx2_nofma": 4}
+    # "cuda" exists only in the integration build (integration/_build/libttref_cuda.so)
+    MODES = {"interpreted": 0, "scalar": 1, "avx2": 2, "avx2_fma": 3, "avx2_nofma": 4, "cuda": 5}
 
     def __init__(self, path=REF_SO):
         if not os.path.exists(path):

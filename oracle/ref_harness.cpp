@@ -32,6 +32,11 @@
 #include "tinytensor/graph/graph.hpp"
 #include "tinytensor/ir/printer.hpp"
 #include "tinytensor/runtime/executor.hpp"
+#ifdef TTREF_WITH_CUDA
+// Built by integration/Makefile against the reference tree with the CompiledCUDA mode
+// added (integration/executor.patch): mode 5 and the device-tensor entry points below.
+#include "tinytensor/runtime/cuda_executable.hpp"
+#endif
 
 using namespace tinytensor;
 
@@ -177,17 +182,22 @@ size_t ttref_ir(void* p, char* buf, size_t cap) {
     return s.size() + 1;
 }
 
-// mode: 0 interpreted, 1 scalar, 2 avx2 (host ISA), 3 avx2_fma, 4 avx2_nofma
+// mode: 0 interpreted, 1 scalar, 2 avx2 (host ISA), 3 avx2_fma, 4 avx2_nofma,
+//       5 cuda (only in the integration build)
 void* ttref_compile(void* p, int mode, int optimize) {
     auto* hg = static_cast<HGraph*>(p);
     try {
         ExecutionMode m = ExecutionMode::Interpreted;
         switch (mode) {
+            case 0: m = ExecutionMode::Interpreted; break;
             case 1: m = ExecutionMode::CompiledScalar; break;
             case 2: m = ExecutionMode::CompiledAVX2; break;
             case 3: m = ExecutionMode::CompiledAVX2_FMA; break;
             case 4: m = ExecutionMode::CompiledAVX2_NoFMA; break;
-            default: break;
+#ifdef TTREF_WITH_CUDA
+            case 5: m = ExecutionMode::CompiledCUDA; break;
+#endif
+            default: throw std::runtime_error("ttref_compile: unknown mode " + std::to_string(mode));
         }
         auto* he = new HExec();
         he->hg = hg;
@@ -283,5 +293,57 @@ double ttref_time_gradients(void* p, int loss, const float* const* inputs, int r
         return -1.0;
     }
 }
+
+#ifdef TTREF_WITH_CUDA
+int ttref_has_cuda() { return 1; }
+
+// Executor::execution_plan / generated_source text (what = 0 plan, 1 source).
+size_t ttref_exec_text(void* e, int what, char* buf, size_t cap) {
+    auto* he = static_cast<HExec*>(e);
+    const std::string s = what == 0 ? he->ex->execution_plan() : he->ex->generated_source();
+    if (buf && cap) {
+        const size_t n = s.size() < cap - 1 ? s.size() : cap - 1;
+        std::memcpy(buf, s.data(), n);
+        buf[n] = '\0';
+    }
+    return s.size() + 1;
+}
+
+// Device-resident run: the inputs are copied to device tensors once, Executor::run
+// takes them (no host staging) and returns device tensors, which are copied back here.
+// With e2 (may be NULL) the first executor's outputs feed the second one's inputs in
+// order, still on the device, and `outputs` receives the second one's results.
+// Returns 0, or -1 with the error text (also when an output is not a device tensor).
+int ttref_run_device(void* e, void* e2, const float* const* inputs, float* const* outputs) {
+    auto* he = static_cast<HExec*>(e);
+    return guarded([&] {
+        std::unordered_map<const Node*, Tensor> feed;
+        const auto& ins = he->hg->g.inputs();
+        for (size_t i = 0; i < ins.size(); ++i) {
+            Tensor t(ins[i]->shape(), DType::Float32);
+            std::memcpy(t.raw_data(), inputs[i], t.nbytes());
+            feed[ins[i]] = cuda_to_device(t);
+        }
+        std::vector<Tensor> outs = he->ex->run(feed);
+        if (e2) {
+            auto* h2 = static_cast<HExec*>(e2);
+            const auto& ins2 = h2->hg->g.inputs();
+            if (ins2.size() != outs.size()) throw std::runtime_error("chain: output/input count mismatch");
+            std::unordered_map<const Node*, Tensor> feed2;
+            for (size_t i = 0; i < ins2.size(); ++i) {
+                if (!cuda_is_device(outs[i])) throw std::runtime_error("chain: an output is not on the device");
+                feed2[ins2[i]] = outs[i];
+            }
+            outs = h2->ex->run(feed2);
+        }
+        for (size_t i = 0; i < outs.size(); ++i) {
+            if (!cuda_is_device(outs[i])) throw std::runtime_error("output " + std::to_string(i) + " is not on the device");
+            Tensor c = cuda_to_host(outs[i]);
+            std::memcpy(outputs[i], c.raw_data(), c.nbytes());
+        }
+        return 0;
+    });
+}
+#endif
 
 }  // extern "C"
