@@ -54,6 +54,32 @@ def test_config2_reductions_8192x4096(cache_dir):
     assert "copy" not in prog.execution_plan()
 
 
+@pytest.mark.parametrize("rows,cols", [(5000, 2048), (4800, 2052), (4737, 4100), (6000, 12288)])
+def test_long_row_reductions_one_block_per_row(rows, cols, cache_dir):
+    """Rows of >= 2048 floats with many rows take the one-CTA-per-row kernel: row lengths
+    that leave a partial 4 KB step, NaN and +-inf in some rows, rows of signed zeros."""
+    rng = np.random.default_rng(rows + cols)
+    x = rng.uniform(-1, 1, (rows, cols)).astype(np.float32)
+    x[3, 17] = np.nan
+    x[5, cols - 1] = np.inf
+    x[6, 0] = -np.inf
+    x[7, :] = -0.0
+    x[8, :] = -0.0
+    x[8, cols - 3] = 0.0
+    g = tt.Graph()
+    nx = g.input([rows, cols])
+    outs = [tt.sum(nx, [1]), tt.mean(nx, [1], keepdims=True), tt.max(nx, [1]), tt.sum(tt.transpose(nx, 0, 1), [0])]
+    got = [t.numpy() for t in tt.compile(g, outputs=outs, cache_dir=cache_dir).run({nx: x})]
+    ref = O.evaluate(g, {nx: x}, outs)
+    assert_bitexact(got[2], ref[2])
+    assert np.signbit(got[2][7]) and not np.signbit(got[2][8])
+    for a, b in ((got[0], ref[0]), (got[1], ref[1]), (got[3], ref[3])):
+        a, b = a.reshape(-1), b.reshape(-1)
+        fin = np.isfinite(b)
+        assert_bitexact(a[~fin], b[~fin])      # NaN / inf rows
+        assert_norm(a[fin], b[fin], REDUCTION_NORM_RTOL)
+
+
 def _gemm(m, n, k, cache_dir, rows=None):
     rng = np.random.default_rng(2)
     a = (rng.standard_normal((m, k)) / np.sqrt(k)).astype(np.float32)

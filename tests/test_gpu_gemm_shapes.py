@@ -146,3 +146,66 @@ def test_batched_transposed_operands(cache_dir):
     b = np.ascontiguousarray(np.transpose(bt, (0, 2, 1)))
     assert_norm(c, O.matmul(a, b), GEMM_FROB_RTOL)
     assert_norm(c, np.matmul(a.astype(np.float64), b.astype(np.float64)), GEMM_FROB_RTOL)
+
+
+@pytest.mark.parametrize("m,n,k", [(20000, 12, 8224), (4099, 3, 256), (64, 16, 128)])
+def test_skinny_n_k_split_at_odd_boundaries(m, n, k, cache_dir):
+    """Row-major X and a contiguous [K][Q] right operand: splits of K whose starts are
+    not multiples of the 128-wide tile, a last tile cut short, rows past the 64-row
+    block, one tile only."""
+    rng = np.random.default_rng(m + 5 * n + k)
+    a, b = _data(rng, (m, k), k), _data(rng, (k, n), k)
+    g = tt.Graph()
+    na, nb = g.input([m, k]), g.input([k, n])
+    prog = tt.compile(g, outputs=[na @ nb], cache_dir=cache_dir)
+    assert "simt_skinny[" in prog.execution_plan()
+    _check(prog.run({na: a, nb: b}).numpy(), a, b, rows=80 if m > 4096 else None)
+
+
+@pytest.mark.parametrize("ep", ["tanh", "relu"])
+def test_skinny_n_epilogue(ep, cache_dir):
+    """An activation of a 10-wide product runs in the skinny kernel's store."""
+    rng = np.random.default_rng(7)
+    m, n, k = 32768, 10, 512
+    a, b = _data(rng, (m, k), 1.0), _data(rng, (k, n), k)
+    g = tt.Graph()
+    na, nb = g.input([m, k]), g.input([k, n])
+    y = tt.tanh(na @ nb) if ep == "tanh" else tt.relu(na @ nb)
+    prog = tt.compile(g, outputs=[y], cache_dir=cache_dir)
+    assert f"+{ep}]" in prog.execution_plan()
+    c = prog.run({na: a, nb: b}).numpy()
+    idx = np.arange(0, m, 97, dtype=np.int64)
+    z = a[idx].astype(np.float64) @ b.astype(np.float64)
+    ref = np.tanh(z) if ep == "tanh" else np.maximum(z, 0.0)
+    assert_norm(c[idx], ref, GEMM_FROB_RTOL)
+
+
+@pytest.mark.parametrize("m,n,k", [(1000, 7, 5000), (4096, 16, 32768), (257, 1, 100)])
+def test_skinny_n_transposed_a_shapes(m, n, k, cache_dir):
+    """A = H^T (rows of H contiguous along M): M past the 256-row block, K not a multiple
+    of the 32-row tile, one and sixteen output columns."""
+    rng = np.random.default_rng(m + n + 3 * k)
+    h, t = _data(rng, (k, m), k), _data(rng, (k, n), k)
+    g = tt.Graph()
+    nh, nt = g.input([k, m]), g.input([k, n])
+    prog = tt.compile(g, outputs=[tt.transpose(nh, 0, 1) @ nt], cache_dir=cache_dir)
+    assert "simt_skinny[" in prog.execution_plan()
+    c = prog.run({nh: h, nt: t}).numpy()
+    _check(c, np.ascontiguousarray(h.T), t, rows=96 if m * k > 1 << 24 else None)
+
+
+def test_skinny_batched_both_layouts(cache_dir):
+    """Batched skinny products (batch 3, each operand with its own batch): row-major A,
+    and A^T as an M-major view."""
+    rng = np.random.default_rng(55)
+    bsz, m, n, k = 3, 2000, 10, 1024
+    a = _data(rng, (bsz, m, k), k)
+    h = _data(rng, (bsz, k, m), k)
+    b = _data(rng, (bsz, k, n), k)
+    g = tt.Graph()
+    na, nh, nb = g.input([bsz, m, k]), g.input([bsz, k, m]), g.input([bsz, k, n])
+    prog = tt.compile(g, outputs=[na @ nb, tt.transpose(nh, 1, 2) @ nb], cache_dir=cache_dir)
+    c1, c2 = [t.numpy() for t in prog.run({na: a, nh: h, nb: b})]
+    for i in range(bsz):
+        _check(c1[i], a[i], b[i])
+        _check(c2[i], np.ascontiguousarray(h[i].T), b[i])

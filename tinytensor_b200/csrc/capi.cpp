@@ -17,6 +17,7 @@ using namespace ttb;
 namespace {
 
 thread_local std::string g_last_error;
+thread_local std::string g_last_message;  // g_last_error without the exception-name prefix
 std::atomic<uint64_t> g_launches{0};
 
 int set_error(int status, const std::string& msg) {
@@ -33,6 +34,7 @@ int set_error(int status, const std::string& msg) {
                                   "RuntimeExecutionError: no device: ",
                                   "InvalidArgument: ",
                                   "CommError: "};
+    g_last_message = msg;
     g_last_error = (status > 0 && status <= 12 ? names[status] : "") + msg;
     return status;
 }
@@ -227,7 +229,7 @@ int tt_compile(const tt_graph* cg, const tt_compile_options* opt, tt_program** o
 
         // Generated kernels: NVRTC -> cubin (cached); loaded unless host-only.
         const bool host_only = (o.flags & TT_FLAG_HOST_ONLY) != 0;
-        if (!host_only && tt_device_init(o.device) != TT_OK) throw Error(TT_ERR_NO_DEVICE, g_last_error);
+        if (!host_only && tt_device_init(o.device) != TT_OK) throw Error(TT_ERR_NO_DEVICE, g_last_message);
         std::vector<std::string> used;
         std::vector<int> used_idx;
         for (size_t i = 0; i < p->plan.regions.size(); ++i)

@@ -423,6 +423,266 @@ __global__ void __launch_bounds__(128) gemm_skinny_async_kernel(
     }
 }
 
+// Skinny products with X read along k (x_sk = 1, 16-B aligned rows) and Y a contiguous
+// [K][Q] block (16-B aligned), Q <= 16: the output layer Y = H.W of a network.  CTA:
+// 256 threads over 8*RW rows and one K range; each stage of a 4-stage cp.async ring
+// holds an X tile (8*RW rows x 128 k) and the matching 128 x Q block of Y.  Warp w owns
+// rows w, w+8, .. of a tile and lane l the four k's 4l..4l+3, so a warp reads each of
+// its rows as one conflict-free 512-B float4 load, and the lane's 4 x Q values of Y
+// (4Q consecutive floats: Q float4 loads from shared memory) are loaded once per tile and
+// used for all RW rows: per tile a warp issues Q + RW loads for 4*RW*Q FMAs, with no
+// padding of Q.  Each lane sums its k's in order (fmaf), the warp then adds the 32
+// lanes' sums by a shuffle tree (every lane ends with the same bits), and split partials
+// are added in split order by the split-K reduce: deterministic.  A split holds at most
+// SK2_MAX_K of K, so a lane's sum has at most SK2_MAX_K / 32 terms.
+#ifndef TT_SK2_RW
+#define TT_SK2_RW 4
+#endif
+constexpr int SK2_RW = TT_SK2_RW, SK2_TR = 8 * SK2_RW, SK2_TK = 128, SK2_ST = 4;
+constexpr int64_t SK2_MAX_K = 8192;
+template <int Q>
+constexpr int sk2_wfloats() {  // Y block per stage, padded to whole 16-B chunks
+    return (SK2_TK * Q + 3) / 4 * 4;
+}
+template <int Q>
+constexpr int sk2_smem() {
+    return SK2_ST * (SK2_TR * SK2_TK + sk2_wfloats<Q>()) * 4;
+}
+
+template <int Q>
+__global__ void __launch_bounds__(256, SK2_RW <= 4 ? 2 : 1) gemm_skinny_k2_kernel(
+    const float* __restrict__ X, const float* __restrict__ Y, float* __restrict__ C, int64_t R, int64_t K,
+    int64_t x_sr, int64_t x_sb, int64_t y_sb, int64_t c_sr, int64_t c_sq, int64_t c_sb, int64_t k_per_split,
+    int ksplit, int epilogue) {
+    constexpr int TR = SK2_TR, TK = SK2_TK, ST = SK2_ST, RW = SK2_RW, WF = sk2_wfloats<Q>();
+    constexpr int STAGE = TR * TK + WF;
+    extern __shared__ __align__(16) float sk2_smem_buf[];  // [ST][X tile | Y block]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * TR;
+    const int64_t bz = blockIdx.y / ksplit;
+    const int64_t kb = static_cast<int64_t>(blockIdx.y - bz * ksplit) * k_per_split;
+    const int64_t ke = K < kb + k_per_split ? K : kb + k_per_split;
+    X += bz * x_sb;
+    Y += bz * y_sb;
+    C += static_cast<int64_t>(blockIdx.y) * c_sb;
+    const int ntiles = ke > kb ? static_cast<int>((ke - kb + TK - 1) / TK) : 0;
+
+    auto issue = [&](int t) {
+        float* xs = sk2_smem_buf + (t % ST) * STAGE;
+        const int64_t k0 = kb + static_cast<int64_t>(t) * TK;
+#pragma unroll
+        for (int i = 0; i < TR * TK / 4 / 256; ++i) {
+            const int e = tid + i * 256;
+            const int rr = e >> 5, c = e & 31;
+            const int64_t r = r0 + rr, k = k0 + 4 * c;
+            int bytes = 0;
+            const float* src = X;
+            if (r < R && k < ke) {
+                bytes = ke - k >= 4 ? 16 : static_cast<int>(4 * (ke - k));
+                src = X + r * x_sr + k;
+            }
+            cp_async16(xs + rr * TK + 4 * c, src, bytes);
+        }
+        // Y rows k0 .. k0+127: 128*Q consecutive floats (zero past the K range)
+        float* ws = xs + TR * TK;
+        const int64_t wlim = (ke - k0) * Q;  // floats of this block inside the K range
+        for (int e = tid; e < WF / 4; e += 256) {
+            const int64_t f = 4 * static_cast<int64_t>(e);
+            const int bytes = f >= wlim ? 0 : (wlim - f >= 4 ? 16 : static_cast<int>(4 * (wlim - f)));
+            cp_async16(ws + 4 * e, bytes ? Y + k0 * Q + f : Y, bytes);
+        }
+    };
+
+    float acc[RW][Q];
+#pragma unroll
+    for (int i = 0; i < RW; ++i)
+#pragma unroll
+        for (int q = 0; q < Q; ++q) acc[i][q] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < ST - 1; ++t) {
+        if (t < ntiles) issue(t);
+        cp_async_commit();
+    }
+    for (int t = 0; t < ntiles; ++t) {
+        cp_async_wait<ST - 2>();
+        __syncthreads();
+        if (t + ST - 1 < ntiles) issue(t + ST - 1);
+        cp_async_commit();
+        const float* xs = sk2_smem_buf + (t % ST) * STAGE;
+        // this lane's 4 k's of Y: floats 4l*Q .. 4l*Q + 4Q - 1 of the block
+        const float4* w4 = reinterpret_cast<const float4*>(xs + TR * TK + 4 * lane * Q);
+        float w[4 * Q];
+#pragma unroll
+        for (int v = 0; v < Q; ++v) {
+            const float4 f = w4[v];
+            w[4 * v] = f.x;
+            w[4 * v + 1] = f.y;
+            w[4 * v + 2] = f.z;
+            w[4 * v + 3] = f.w;
+        }
+#pragma unroll
+        for (int i = 0; i < RW; ++i) {
+            const float4 x = *reinterpret_cast<const float4*>(xs + (warp + 8 * i) * TK + 4 * lane);
+#pragma unroll
+            for (int q = 0; q < Q; ++q) {
+                float a = acc[i][q];
+                a = fmaf(x.x, w[q], a);
+                a = fmaf(x.y, w[Q + q], a);
+                a = fmaf(x.z, w[2 * Q + q], a);
+                a = fmaf(x.w, w[3 * Q + q], a);
+                acc[i][q] = a;
+            }
+        }
+    }
+    cp_async_wait<0>();
+#pragma unroll
+    for (int i = 0; i < RW; ++i) {
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            float v = acc[i][q];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            const int64_t r = r0 + warp + 8 * i;
+            if (lane == (i * Q + q) % 32 && r < R) C[r * c_sr + q * c_sq] = gemm_epilogue(v, epilogue);
+        }
+    }
+}
+
+// Skinny products with X read along r (x_sr = 1, x_sk % 4 == 0, 16-B aligned): the
+// weight gradient dW = H^T.dY of an output layer, H row-major.  CTA: 256 threads over
+// 256 r and one K range; X tiles (32 k x 256 r, 32 KB) and Y tiles (32 k x Q, padded to
+// QP) stream through a 3-stage cp.async ring.  Warp w owns r-half w & 1 (128 r, lane l
+// the 4 r's 4l..4l+3) and the k's kk = w >> 1 (mod 4) of a tile: per k one conflict-free
+// float4 load of X, QP/4 broadcast float4 loads of Y and 4Q FMAs.  Each lane sums its
+// k's in order, the four k-groups' sums are then added in group order through shared
+// memory, and split partials in split order: deterministic.  A split holds at most
+// SR2_MAX_K of K (a lane's sum has at most SR2_MAX_K / 4 terms).
+constexpr int SR2_TR = 256, SR2_TK = 32, SR2_ST = 3;
+constexpr int64_t SR2_MAX_K = 2048;
+
+template <int Q>
+constexpr int sr2_qp() {
+    return (Q + 3) / 4 * 4;
+}
+template <int Q>
+constexpr int sr2_smem() {
+    return SR2_ST * (SR2_TK * SR2_TR + SR2_TK * sr2_qp<Q>()) * 4;
+}
+
+template <int Q>
+__global__ void __launch_bounds__(256, 2) gemm_skinny_r2_kernel(
+    const float* __restrict__ X, const float* __restrict__ Y, float* __restrict__ C, int64_t R, int64_t K,
+    int64_t x_sk, int64_t x_sb, int64_t y_sk, int64_t y_sq, int64_t y_sb, int64_t c_sr, int64_t c_sq, int64_t c_sb,
+    int64_t k_per_split, int ksplit, int epilogue) {
+    constexpr int TR = SR2_TR, TK = SR2_TK, ST = SR2_ST, QP = sr2_qp<Q>();
+    extern __shared__ __align__(16) float sr2_smem[];
+    float* Xs = sr2_smem;                 // [ST][TK][TR]
+    float* Ys = sr2_smem + ST * TK * TR;  // [ST][TK][QP]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rh = warp & 1, kg = warp >> 1;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * TR;
+    const int64_t bz = blockIdx.y / ksplit;
+    const int64_t kb = static_cast<int64_t>(blockIdx.y - bz * ksplit) * k_per_split;
+    const int64_t ke = K < kb + k_per_split ? K : kb + k_per_split;
+    X += bz * x_sb;
+    Y += bz * y_sb;
+    C += static_cast<int64_t>(blockIdx.y) * c_sb;
+    const int ntiles = ke > kb ? static_cast<int>((ke - kb + TK - 1) / TK) : 0;
+
+    auto issue = [&](int t) {
+        const int s = t % ST;
+        float* xs = Xs + s * TK * TR;
+        const int64_t k0 = kb + static_cast<int64_t>(t) * TK;
+#pragma unroll
+        for (int i = 0; i < TK * TR / 4 / 256; ++i) {
+            const int e = tid + i * 256;
+            const int kk = e >> 6, c = e & 63;
+            const int64_t k = k0 + kk, r = r0 + 4 * c;
+            int bytes = 0;
+            const float* src = X;
+            if (k < ke && r < R) {
+                bytes = R - r >= 4 ? 16 : static_cast<int>(4 * (R - r));
+                src = X + k * x_sk + r;
+            }
+            cp_async16(xs + kk * TR + 4 * c, src, bytes);
+        }
+        float* ys = Ys + s * TK * QP;
+        for (int e = tid; e < TK * QP; e += 256) {
+            const int kk = e / QP, q = e - kk * QP;
+            const int64_t k = k0 + kk;
+            const bool in = k < ke && q < Q;
+            cp_async4(ys + e, in ? Y + k * y_sk + q * y_sq : Y, in ? 4 : 0);
+        }
+    };
+
+    float acc[4][Q];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int q = 0; q < Q; ++q) acc[j][q] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < ST - 1; ++t) {
+        if (t < ntiles) issue(t);
+        cp_async_commit();
+    }
+    for (int t = 0; t < ntiles; ++t) {
+        cp_async_wait<ST - 2>();
+        __syncthreads();
+        if (t + ST - 1 < ntiles) issue(t + ST - 1);
+        cp_async_commit();
+        const int s = t % ST;
+        const float* xs = Xs + s * TK * TR + rh * 128 + 4 * lane;
+        const float* ys = Ys + s * TK * QP;
+#pragma unroll 4
+        for (int kk = kg; kk < TK; kk += 4) {
+            const float4 x = *reinterpret_cast<const float4*>(xs + kk * TR);
+            const float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int q4 = 0; q4 < QP / 4; ++q4) {
+                const float4 y = *reinterpret_cast<const float4*>(ys + kk * QP + 4 * q4);
+                const float yv[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    if (4 * q4 + u < Q) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) acc[j][4 * q4 + u] = fmaf(xv[j], yv[u], acc[j][4 * q4 + u]);
+                    }
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    // k-groups 1..3 park their sums; group 0 adds them in group order and stores
+    float* red = sr2_smem;  // [3][2][32][4][Q] floats, inside the ring
+    if (kg > 0) {
+        float* d = red + ((((kg - 1) * 2 + rh) * 32 + lane) * 4) * Q;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int q = 0; q < Q; ++q) d[j * Q + q] = acc[j][q];
+    }
+    __syncthreads();
+    if (kg == 0) {
+#pragma unroll
+        for (int g = 0; g < 3; ++g) {
+            const float* d = red + (((g * 2 + rh) * 32 + lane) * 4) * Q;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int q = 0; q < Q; ++q) acc[j][q] = __fadd_rn(acc[j][q], d[j * Q + q]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t r = r0 + rh * 128 + 4 * lane + j;
+            if (r < R) {
+#pragma unroll
+                for (int q = 0; q < Q; ++q) C[r * c_sr + q * c_sq] = gemm_epilogue(acc[j][q], epilogue);
+            }
+        }
+    }
+}
+
 // Products with K <= 16 (bound by writing C).  A CTA owns one 128-column strip of C:
 // it stages B (K x 128) in shared memory once and keeps each thread's 4 columns of it
 // in registers (KP <= 16 float4s, K padded with zeros), then walks row blocks of 64
@@ -597,13 +857,77 @@ void launch_skinny_async(const SkinnyView& v, const GemmDesc& d, float* out, int
     else launch_skinny_async_t<16, XMAJ>(v, d, out, out_sb, grid, st);
 }
 
+// Which skinny kernel a view's strides select (alignment is checked again at launch).
+enum SkinnyKind { SK_OLD = 0, SK_K2 = 1, SK_R2 = 2 };
+SkinnyKind skinny_kind(const SkinnyView& v) {
+    if (v.Q > 16) return SK_OLD;
+    if (v.x_sk == 1 && v.x_sr % 4 == 0 && v.y_sq == 1 && v.y_sk == v.Q) return SK_K2;
+    if (v.x_sr == 1 && v.x_sk % 4 == 0) return SK_R2;
+    return SK_OLD;
+}
+
+template <int Q>
+void launch_k2_t(const SkinnyView& v, const GemmDesc& d, float* out, int64_t out_sb, cudaStream_t st) {
+    static bool attr = [] {
+        return cudaFuncSetAttribute(gemm_skinny_k2_kernel<Q>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    sk2_smem<Q>()) == cudaSuccess;
+    }();
+    (void)attr;
+    dim3 grid(static_cast<unsigned>((v.R + SK2_TR - 1) / SK2_TR), static_cast<unsigned>(d.batch * d.ksplit));
+    gemm_skinny_k2_kernel<Q><<<grid, 256, sk2_smem<Q>(), st>>>(v.X, v.Y, out, v.R, d.K, v.x_sr, v.x_sb, v.y_sb, v.c_sr,
+                                                         v.c_sq, out_sb, skinny_k_per_split(d), d.ksplit,
+                                                         d.ksplit > 1 ? EP_NONE : d.epilogue);
+}
+
+template <int Q>
+void launch_r2_t(const SkinnyView& v, const GemmDesc& d, float* out, int64_t out_sb, cudaStream_t st) {
+    static bool attr = [] {
+        return cudaFuncSetAttribute(gemm_skinny_r2_kernel<Q>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    sr2_smem<Q>()) == cudaSuccess;
+    }();
+    (void)attr;
+    dim3 grid(static_cast<unsigned>((v.R + SR2_TR - 1) / SR2_TR), static_cast<unsigned>(d.batch * d.ksplit));
+    gemm_skinny_r2_kernel<Q><<<grid, 256, sr2_smem<Q>(), st>>>(v.X, v.Y, out, v.R, d.K, v.x_sk, v.x_sb, v.y_sk, v.y_sq,
+                                                              v.y_sb, v.c_sr, v.c_sq, out_sb, skinny_k_per_split(d),
+                                                              d.ksplit, d.ksplit > 1 ? EP_NONE : d.epilogue);
+}
+
+#define TT_SKINNY_Q_CASES(F) \
+    F(1) F(2) F(3) F(4) F(5) F(6) F(7) F(8) F(9) F(10) F(11) F(12) F(13) F(14) F(15) F(16)
+
+void launch_k2(const SkinnyView& v, const GemmDesc& d, float* out, int64_t out_sb, cudaStream_t st) {
+    switch (v.Q) {
+#define TT_K2_CASE(q) \
+    case q: launch_k2_t<q>(v, d, out, out_sb, st); break;
+        TT_SKINNY_Q_CASES(TT_K2_CASE)
+#undef TT_K2_CASE
+        default: break;
+    }
+}
+
+void launch_r2(const SkinnyView& v, const GemmDesc& d, float* out, int64_t out_sb, cudaStream_t st) {
+    switch (v.Q) {
+#define TT_R2_CASE(q) \
+    case q: launch_r2_t<q>(v, d, out, out_sb, st); break;
+        TT_SKINNY_Q_CASES(TT_R2_CASE)
+#undef TT_R2_CASE
+        default: break;
+    }
+}
+
 int launch_skinny(const GemmDesc& d, const float* A, const float* B, float* C, void* scratch, cudaStream_t st) {
     const SkinnyView v = skinny_view(d, A, B);
     const bool x16 = (reinterpret_cast<uintptr_t>(v.X) & 15) == 0 && (d.batch == 1 || v.x_sb % 4 == 0);
+    const bool y16 = (reinterpret_cast<uintptr_t>(v.Y) & 15) == 0 && (d.batch == 1 || v.y_sb % 4 == 0);
     float* out = d.ksplit > 1 ? static_cast<float*>(scratch) : C;
     const int64_t out_sb = d.ksplit > 1 ? d.M * d.N : d.c_sb;
     dim3 grid(static_cast<unsigned>((v.R + 127) / 128), static_cast<unsigned>(d.batch * d.ksplit));
-    if (x16 && v.x_sk == 1 && v.x_sr % 4 == 0) {
+    const SkinnyKind kind = skinny_kind(v);
+    if (x16 && y16 && kind == SK_K2) {
+        launch_k2(v, d, out, out_sb, st);
+    } else if (x16 && kind == SK_R2) {
+        launch_r2(v, d, out, out_sb, st);
+    } else if (x16 && v.x_sk == 1 && v.x_sr % 4 == 0) {
         launch_skinny_async<XM_K>(v, d, out, out_sb, grid, st);
     } else if (x16 && v.x_sr == 1 && v.x_sk % 4 == 0) {
         launch_skinny_async<XM_R>(v, d, out, out_sb, grid, st);
@@ -617,9 +941,49 @@ int launch_skinny(const GemmDesc& d, const float* A, const float* B, float* C, v
     return launch_splitk_reduce(out, C, d.M * d.N, d.ksplit, d.batch, d.c_sb, d.epilogue, st);
 }
 
-// Split-K of the skinny kernels: enough CTAs for ~2 waves of 3 per SM, each split >= 256 of K.
+// Split-K of the skinny kernels.  K2 / R2 (one / two resident CTAs per SM): a wave model
+// like the tensor-core planner's — waves x (tiles per split + a ramp of ~2 tiles) plus
+// the partials' extra HBM traffic in tile times — under the kernels' cap on K per split.
+// Others: enough CTAs for ~2 waves of 3 per SM, each split >= 256 of K.
+int64_t plan_skinny_split(int64_t ctas, int64_t K, int64_t tk, int64_t max_k, int64_t slots, double tile_bytes_hbm,
+                          double out_bytes, int64_t batch) {
+    const int64_t ntk = (K + tk - 1) / tk;
+    const int64_t smin = (K + max_k - 1) / max_k;
+    int64_t best = smin;
+    double best_cost = -1.0;
+    for (int64_t ks = smin; ks <= smin + 256 && ks <= ntk && ks * batch <= 65535; ++ks) {
+        const int64_t per = (ntk + ks - 1) / ks;
+        const int64_t waves = (ctas * ks + slots - 1) / slots;
+        double cost = static_cast<double>(waves) * (static_cast<double>(per) + 2.0);
+        if (ks > 1) cost += 2.0 * static_cast<double>(ks) * out_bytes / tile_bytes_hbm;
+        if (best_cost < 0.0 || cost < best_cost) {
+            best_cost = cost;
+            best = ks;
+        }
+    }
+    return best;
+}
+
 void plan_skinny(GemmDesc& d) {
     const int64_t R = d.algo == ALGO_SKINNY_T ? d.N : d.M;
+    const SkinnyView v = skinny_view(d, nullptr, nullptr);
+    const double out_bytes = static_cast<double>(d.M) * static_cast<double>(d.N) * 4.0 * static_cast<double>(d.batch);
+    // HBM bytes moved (whole GPU) while one CTA streams one tile: 32 KB tiles at the
+    // per-SM share of ~6.5 TB/s, shared by the CTAs resident on the SM
+    const SkinnyKind kind = skinny_kind(v);
+    if (kind == SK_K2) {
+        const int64_t per_sm = SK2_RW <= 4 ? 2 : 1;
+        const double tile_bytes = static_cast<double>(SK2_TR * SK2_TK * 4);
+        d.ksplit = static_cast<int>(plan_skinny_split((R + SK2_TR - 1) / SK2_TR * d.batch, d.K, SK2_TK, SK2_MAX_K,
+                                                      148 * per_sm, 148.0 * static_cast<double>(per_sm) * tile_bytes,
+                                                      out_bytes, d.batch));
+        return;
+    }
+    if (kind == SK_R2) {
+        d.ksplit = static_cast<int>(plan_skinny_split((R + SR2_TR - 1) / SR2_TR * d.batch, d.K, SR2_TK, SR2_MAX_K,
+                                                      296, 2.0 * 148.0 * 32768.0, out_bytes, d.batch));
+        return;
+    }
     const int64_t ctas = (R + 127) / 128 * d.batch;
     int64_t ks = 1;
     if (ctas < 148 * 6) {

@@ -82,6 +82,7 @@ struct TcParams {
     int a_batched, b_batched;
     int ksplit, kb_per_split, chunk_kb;
     int tiles_m, tiles_n, n_units;  // pair kernel: 256x256 tiles and work units (tiles x batch x splits)
+    int group_m;                    // pair kernel: M-tiles per group of the unit order (see pair_unit)
     int epilogue;        // applied here only when ksplit == 1
     int* status;
 };
@@ -463,7 +464,14 @@ constexpr uint32_t kIdescPair = (1u << 4) | (2u << 7) | (2u << 10) | (static_cas
                                 (static_cast<uint32_t>(256 >> 4) << 24);
 
 // Work unit u of the persistent pair kernel: output pair-tile (tm, tn) of batch/split zz.
-// N-tiles vary fastest, so the clusters running at the same time share A row tiles.
+// Within a batch/split the tiles are taken in groups of group_m M-tiles: inside a group
+// M-tiles vary fastest, then N-tiles, and every other group walks its N-tiles backwards.
+// The clusters running at one time hold consecutive units, so they cover a block of
+// about group_m x (clusters / group_m) tiles instead of a few whole rows of tiles: fewer
+// A and B panels are streamed at once (each read from DRAM once and shared through L2
+// by the tiles of its row or column), and the B panels at the turn between two groups
+// are still in L2.  group_m = 1 walks rows of tiles (N-tiles fastest), alternating
+// direction.
 struct PairUnit {
     int n0, m0, nb0, zb_all, za, zb, kb0, kcount;
 };
@@ -472,7 +480,12 @@ __device__ __forceinline__ PairUnit pair_unit(const TcParams& p, int u, uint32_t
     PairUnit w;
     const int per_z = p.tiles_m * p.tiles_n;
     const int zz = u / per_z, rem = u - zz * per_z;
-    const int tm = rem / p.tiles_n, tn = rem - tm * p.tiles_n;
+    const int span = p.group_m * p.tiles_n;  // units of a full group
+    const int g = rem / span, first = g * p.group_m;
+    const int gsz = min(p.group_m, p.tiles_m - first);
+    const int i = rem - g * span;
+    const int tm = first + i % gsz;
+    const int tn = (g & 1) ? p.tiles_n - 1 - i / gsz : i / gsz;
     w.n0 = tn * 256;
     w.m0 = tm * 256 + static_cast<int>(rank) * 128;
     w.nb0 = w.n0 + static_cast<int>(rank) * 128;
@@ -967,6 +980,9 @@ bool gemm_tc_supported(const GemmDesc& d) {
 #ifndef TT_GEMM_PAIR
 #define TT_GEMM_PAIR 1
 #endif
+#ifndef TT_GEMM_GROUP_M
+#define TT_GEMM_GROUP_M 8
+#endif
 void gemm_tc_plan(GemmDesc& d) {
     d.bk = TT_GEMM_BK;
     d.chunk_kb = 256 / d.bk;  // 256 values of K per TMEM chunk
@@ -1044,6 +1060,7 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
     encode_operand(&m_blo, blo, d.N, d.K, bp, bk, b_rows);
     const int64_t nkb = (d.K + bk - 1) / bk;
     TcParams p;
+    p.group_m = 1;
     p.M = static_cast<int>(d.M);
     p.N = static_cast<int>(d.N);
     p.K = static_cast<int>(d.K);
@@ -1068,6 +1085,12 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
         p.tiles_m = static_cast<int>((d.M + 255) / 256);
         p.tiles_n = static_cast<int>((d.N + 255) / 256);
         p.n_units = static_cast<int>(p.tiles_m * p.tiles_n * d.batch * d.ksplit);
+        // Groups of 8 tile rows when rows of tiles are long: at 8192^3 (32 tile columns)
+        // the 74 clusters of a wave would otherwise stream 32 B panels and 2-3 A panels at
+        // once (measured 263-266 -> 278-282 TFLOP/s with groups).  At 16 tile columns (the
+        // MLP's 4096-wide products) groups read 3-11 % fewer DRAM bytes but ran within
+        // +-1 % of rows (1 % slower at K = 1024), so rows stay there.
+        p.group_m = p.tiles_n > 16 ? TT_GEMM_GROUP_M : 1;
         rc = launch_pair<32>(m_ahi, m_alo, m_bhi, m_blo, p, st);
     } else {
         dim3 grid(static_cast<unsigned>((d.N + BN - 1) / BN), static_cast<unsigned>((d.M + BM - 1) / BM),

@@ -114,6 +114,96 @@ __global__ void __launch_bounds__(kThreads) reduce_row_kernel(const float* __res
     }
 }
 
+// ROW with long rows (R >= kCtaRowMin, float4, no split): one CTA per row.  The 8 warps
+// read consecutive 4 KB pieces of one row and the CTAs are dispatched in row order, so
+// the CTAs resident at one time stream one contiguous window of X, 16 KB runs side by
+// side.  (A warp per row puts a stream on every row at once, 8192 streams 16 KB apart
+// for [8192, 4096], which costs HBM row-buffer locality: 0.80 of the copy bandwidth
+// against 0.90 here.  A persistent-CTA variant streaming 16 KB chunks through a cp.async
+// ring ran at 0.81 at best.)  Registers stay at 32 so that 8 CTAs fit per SM: a second
+// accumulator chain per thread (40 registers, 6 CTAs per SM) cost 10 %.
+// Per-thread partials are merged by a warp shuffle tree, then the 8 warp results in warp
+// order: a fixed order, so the result is deterministic.
+// max takes the hardware's NaN-propagating maximum (max.NaN.f32, one instruction per
+// element).  Its choice between -0 and +0 is not relied on: a row whose maximum is a
+// zero is scanned again for a +0 (IEEE 754-2019 maximum: -0 < +0).
+constexpr int64_t kCtaRowMin = 2048;
+
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+
+template <int OP>
+struct RowAcc : Acc<OP> {};
+template <>
+struct RowAcc<RO_MAX> {
+    float v = -INFINITY;
+    __device__ void add(float x) { v = max_nan(v, x); }
+    __device__ double get() const { return static_cast<double>(v); }
+};
+
+template <int OP>
+__global__ void __launch_bounds__(kThreads, 8) reduce_row_cta_kernel(const float* __restrict__ x, float* __restrict__ out,
+                                                                   int64_t R, int64_t s_outer, float scale) {
+    __shared__ double wpart[kThreads / 32];
+    const int64_t row = blockIdx.x;
+    const float4* r4 = reinterpret_cast<const float4*>(x + row * s_outer);
+    const int nvec = static_cast<int>(R / 4);
+    RowAcc<OP> acc;
+    int v = threadIdx.x;
+    for (; v + 3 * kThreads < nvec; v += 4 * kThreads) {
+        float4 q[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) q[u] = __ldg(r4 + v + u * kThreads);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            acc.add(q[u].x);
+            acc.add(q[u].y);
+            acc.add(q[u].z);
+            acc.add(q[u].w);
+        }
+    }
+    for (; v < nvec; v += kThreads) {
+        const float4 q = __ldg(r4 + v);
+        acc.add(q.x);
+        acc.add(q.y);
+        acc.add(q.z);
+        acc.add(q.w);
+    }
+    double r;
+    if (OP == RO_MAX) {
+        float m = static_cast<float>(acc.get());
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
+        r = static_cast<double>(m);
+    } else {
+        r = warp_merge<OP>(acc.get());
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) wpart[warp] = r;
+    __syncthreads();
+    if (OP == RO_MAX) {
+        float m = -INFINITY;
+        for (int w = 0; w < kThreads / 32; ++w) m = max_nan(m, static_cast<float>(wpart[w]));
+        if (m == 0.0f) {  // -0 or +0: +0 if the row holds a +0 (all threads agree on m)
+            int plus = 0;
+            for (int i = threadIdx.x; i < nvec; i += kThreads) {
+                const float4 q = __ldg(r4 + i);
+                plus |= (__float_as_uint(q.x) == 0u) | (__float_as_uint(q.y) == 0u) | (__float_as_uint(q.z) == 0u) |
+                        (__float_as_uint(q.w) == 0u);
+            }
+            m = __syncthreads_or(plus) ? 0.0f : -0.0f;
+        }
+        if (threadIdx.x == 0) out[row] = m;
+    } else if (threadIdx.x == 0) {
+        Acc<OP> t;
+        for (int w = 0; w < kThreads / 32; ++w) t.merge(wpart[w]);
+        out[row] = finish<OP>(t.get(), scale);
+    }
+}
+
 // COL: one thread per VEC consecutive columns and one split of the rows.
 template <int OP, int VEC>
 __global__ void __launch_bounds__(kThreads) reduce_col_kernel(const float* __restrict__ x, float* __restrict__ out,
@@ -240,7 +330,10 @@ int launch_op(const ReduceDesc& d, const float* in, float* out, void* scratch, v
         fill_kernel<<<static_cast<unsigned>((d.outer + kThreads - 1) / kThreads), kThreads, 0, st>>>(out, d.outer, v);
         return static_cast<int>(cudaGetLastError());
     }
-    if (d.kind == RK_ROW) {
+    if (d.kind == RK_ROW && d.vec == 4 && d.splits == 1 && d.R >= kCtaRowMin) {
+        reduce_row_cta_kernel<OP><<<static_cast<unsigned>(d.outer), kThreads, 0, st>>>(x, out, d.R, d.s_outer,
+                                                                                      d.mean_scale);
+    } else if (d.kind == RK_ROW) {
         int64_t warps = d.outer * d.splits;
         unsigned blocks = static_cast<unsigned>((warps * 32 + kThreads - 1) / kThreads);
         if (d.vec == 4)
