@@ -194,7 +194,7 @@ def run_b200(args):
     dx, dt = tt.DeviceBuffer.from_numpy(xs), tt.DeviceBuffer.from_numpy(ts)
     dw = [tt.DeviceBuffer.from_numpy(a) for a in w]
     comm = tt.Communicator.from_torch_distributed(local) if world > 1 else None
-    trainer = tt.DataParallelSGD(prog, dw, lr=LR, comm=comm)
+    trainer = tt.DataParallelSGD(prog, dw, lr=LR, comm=comm, early_update=not args.no_early_update)
     dloss = trainer.loss
 
     def step():
@@ -548,6 +548,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-components", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-early-update", action="store_true",
+                    help="update the parameters after the whole exchange instead of as each one is ready")
     ap.add_argument("--workload", default="mlp", choices=["mlp", "gemm", "elementwise", "reduce"],
                     help="mlp: the headline step; the others time one compiled program (profiling cases)")
     ap.add_argument("--size", default=None, help="gemm: M,N,K; elementwise: n (an n x n chain); reduce: R,C")

@@ -194,6 +194,15 @@ int tt_program_set_output_events(tt_program* p, void* const* events, int32_t n);
 /* Index of the launch after which output `output` is complete (-1: before the first),
  * i.e. the order in which the output events fire. */
 int tt_program_output_step(tt_program* p, int32_t output, int32_t* step);
+/* Input-released events (no counterpart in the reference: its inputs are host tensors
+ * copied per call).  events[k] (a tt_event_create handle, or NULL) is recorded on the
+ * run's stream as soon as the last launch reading input k is complete, so the caller
+ * may overwrite that device buffer from another stream — e.g. the SGD update of a
+ * parameter whose gradient is already exchanged — while the rest of the program still
+ * runs.  n <= number of inputs; n = 0 clears.  The caller keeps the handles alive. */
+int tt_program_set_input_events(tt_program* p, void* const* events, int32_t n);
+/* Index of the launch after which input `input` is no longer read (-1: never read). */
+int tt_program_input_step(tt_program* p, int32_t input, int32_t* step);
 
 /* ---- buffers (plain cudaMalloc / cudaMallocHost / cudaMemcpyAsync) ---- */
 enum tt_copy { TT_H2D = 1, TT_D2H = 2, TT_D2D = 3 };

@@ -261,6 +261,12 @@ def test_gradients_are_scheduled_early_with_output_steps(cache_dir):
     assert dw3_s < dw2_s < dw1_s
     dh1 = [i for i, l in enumerate(launches) if "[64x256x256" in l and "B:K" in l]
     assert dh1 and dw2_s < dh1[0]
+    # input_steps(): the launch after which each input is no longer read — W1 only by the
+    # first GEMM, W2 last by dH1 = dZ2 W2^T (after dW2 is out), X last by dW1 = X^T dZ1
+    x_s, t_s, w1_s, w2_s, w3_s = p.input_steps()
+    assert w1_s == 0 and x_s == dw1_s == len(launches) - 1
+    assert w2_s == dh1[0] and dw2_s < w2_s
+    assert 0 <= t_s < dw3_s and 0 <= w3_s < len(launches)
 
 
 def test_independent_gemms_run_side_by_side_without_sharing_memory(cache_dir):

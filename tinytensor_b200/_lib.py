@@ -160,6 +160,8 @@ SIGNATURES = {
     "tt_program_destroy": (ctypes.c_int, [_VP]),
     "tt_program_set_output_events": (ctypes.c_int, [_VP, ctypes.POINTER(_VP), _I32]),
     "tt_program_output_step": (ctypes.c_int, [_VP, _I32, ctypes.POINTER(_I32)]),
+    "tt_program_set_input_events": (ctypes.c_int, [_VP, ctypes.POINTER(_VP), _I32]),
+    "tt_program_input_step": (ctypes.c_int, [_VP, _I32, ctypes.POINTER(_I32)]),
     "tt_device_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(_VP)]),
     "tt_device_free": (ctypes.c_int, [_VP]),
     "tt_host_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(_VP)]),

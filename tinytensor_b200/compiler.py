@@ -322,6 +322,24 @@ class CompiledProgram:
         arr = (ctypes.c_void_p * max(1, n))(*[e.handle if e is not None else None for e in self._out_events])
         _lib.check(_lib.lib.tt_program_set_output_events(self._h, arr, n))
 
+    def set_input_events(self, events) -> None:
+        """events[k] (an Event or None) is recorded on the run's stream as soon as the
+        last launch reading input k is done: the input's buffer may then be overwritten
+        (e.g. a parameter update) while the rest of the program still runs."""
+        self._in_events = list(events)
+        n = len(self._in_events)
+        arr = (ctypes.c_void_p * max(1, n))(*[e.handle if e is not None else None for e in self._in_events])
+        _lib.check(_lib.lib.tt_program_set_input_events(self._h, arr, n))
+
+    def input_steps(self):
+        """Per input, the launch after which it is no longer read (-1: never read)."""
+        out = []
+        for k in range(self.num_inputs):
+            s = ctypes.c_int32()
+            _lib.check(_lib.lib.tt_program_input_step(self._h, k, ctypes.byref(s)))
+            out.append(s.value)
+        return out
+
     def output_steps(self):
         """Per output, the launch after which it is complete (the order its event fires)."""
         out = []

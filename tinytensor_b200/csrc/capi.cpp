@@ -103,6 +103,7 @@ struct tt_program {
     bool prof_pending = false;
     bool has_tc = false;
     std::vector<cudaEvent_t> out_events;  // caller's events, recorded when an output is complete
+    std::vector<cudaEvent_t> in_events;   // caller's events, recorded after an input's last reader
     cudaStream_t side = nullptr;          // second stream for concurrent GEMM pairs
     cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     std::mutex run_mutex;
@@ -335,6 +336,9 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
         for (size_t k = 0; k < p->out_events.size(); ++k)
             if (p->out_events[k] && pl.output_step[k] == step)
                 check_cuda(cudaEventRecord(p->out_events[k], st), "cudaEventRecord(output)");
+        for (size_t k = 0; k < p->in_events.size(); ++k)
+            if (p->in_events[k] && pl.input_last_step[k] == step)
+                check_cuda(cudaEventRecord(p->in_events[k], st), "cudaEventRecord(input)");
     };
     auto launch_one = [&](size_t s, cudaStream_t st) {
         const Launch& L = pl.launches[s];
@@ -492,6 +496,26 @@ int tt_program_set_output_events(tt_program* p, void* const* events, int32_t n) 
         std::lock_guard<std::mutex> lk(p->run_mutex);
         p->out_events.assign(static_cast<size_t>(n), nullptr);
         for (int32_t k = 0; k < n; ++k) p->out_events[static_cast<size_t>(k)] = static_cast<cudaEvent_t>(events[k]);
+    });
+}
+
+int tt_program_set_input_events(tt_program* p, void* const* events, int32_t n) {
+    return guarded([&] {
+        if (!p) fail(TT_ERR_INVALID, "null program");
+        if (n < 0 || static_cast<size_t>(n) > p->in_shapes.size() || (n > 0 && !events))
+            fail(TT_ERR_INVALID, "events: expected at most " + std::to_string(p->in_shapes.size()) + " entries");
+        std::lock_guard<std::mutex> lk(p->run_mutex);
+        p->in_events.assign(static_cast<size_t>(n), nullptr);
+        for (int32_t k = 0; k < n; ++k) p->in_events[static_cast<size_t>(k)] = static_cast<cudaEvent_t>(events[k]);
+    });
+}
+
+int tt_program_input_step(tt_program* p, int32_t input, int32_t* step) {
+    return guarded([&] {
+        if (!p || !step) fail(TT_ERR_INVALID, "null argument");
+        if (input < 0 || static_cast<size_t>(input) >= p->plan.input_last_step.size())
+            fail(TT_ERR_INVALID, "input index out of range");
+        *step = p->plan.input_last_step[static_cast<size_t>(input)];
     });
 }
 

@@ -1046,6 +1046,27 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
     }
     (void)out_copy_region;
     // launch after which each graph output is complete (its last writer)
+    // last launch that reads each graph input's buffer (a caller may overwrite the input,
+    // e.g. a parameter update, once that launch is done)
+    p.input_last_step.assign(g.inputs.size(), -1);
+    {
+        std::map<int, size_t> input_of;
+        for (size_t k = 0; k < g.inputs.size(); ++k) input_of[g.inputs[k]] = k;
+        for (size_t s = 0; s < p.launches.size(); ++s) {
+            const Launch& L = p.launches[s];
+            auto mark = [&](int root) {
+                auto it = input_of.find(root);
+                if (it != input_of.end()) p.input_last_step[it->second] = static_cast<int>(s);
+            };
+            if (L.type == LT_REGION) {
+                for (const Access& a : p.regions[static_cast<size_t>(L.region)].ext_access)
+                    if (!a.imm) mark(a.node);
+            } else {
+                mark(L.in_node);
+                if (L.in_node2 >= 0) mark(L.in_node2);
+            }
+        }
+    }
     p.output_step.assign(g.outputs.size(), -1);
     for (size_t s = 0; s < p.launches.size(); ++s) {
         const Launch& L = p.launches[s];

@@ -39,6 +39,7 @@ struct Plan {
     // per graph output: index of the launch after which it is complete (-1: written by
     // no launch, complete when the program starts)
     std::vector<int> output_step;
+    std::vector<int> input_last_step;  // per graph input: the last launch reading it (-1: none)
 };
 
 struct ScheduleOptions {

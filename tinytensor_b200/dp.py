@@ -104,12 +104,17 @@ class DataParallelSGD:
     program's output events; the scheduler runs output-producing launches as early as
     their inputs allow), in the order the program produces them — the same on every
     rank — so the exchange of one layer's gradient overlaps the backward pass of the
-    layers before it.  The update then waits for the exchange and applies lr / world.
-    With comm=None (one process) the step is the plain single-GPU step; overlap=False
-    all-reduces the whole buffer once after the program.
+    layers before it.  With early_update, each parameter is then updated on the same
+    side stream as soon as its gradient is exchanged and the program's last launch that
+    reads the parameter is done (the program's input-released events), so only the last
+    layer's exchange and update remain after the backward pass; the next step waits for
+    all updates.  Updates apply lr / world.  With comm=None (one process) there is no
+    exchange (early updates still overlap the backward pass); overlap=False all-reduces
+    the whole buffer once after the program and updates after that.
     """
 
-    def __init__(self, program, params, lr: float = 0.01, momentum: float = 0.0, comm=None, overlap: bool = True):
+    def __init__(self, program, params, lr: float = 0.01, momentum: float = 0.0, comm=None, overlap: bool = True,
+                 early_update: bool = True):
         from .compiler import DeviceBuffer, Event, Stream
         from .optim import SGD
 
@@ -124,7 +129,8 @@ class DataParallelSGD:
         self.loss = DeviceBuffer([])
         self.opt = SGD(self.params, lr=lr, momentum=momentum)
         self.overlap = bool(overlap and comm is not None and comm.world > 1)
-        if self.overlap:
+        self.early_update = bool(early_update and (self.overlap or comm is None or comm.world == 1))
+        if self.overlap or self.early_update:
             self.comm_stream = Stream()
             self.ready = [Event() for _ in self.params]
             self.exchanged = Event()
@@ -132,6 +138,11 @@ class DataParallelSGD:
             steps = program.output_steps()[1:1 + len(self.params)]
             # exchange order = production order (ties: parameter order), identical on all ranks
             self.order = sorted(range(len(self.params)), key=lambda i: (steps[i], i))
+        if self.early_update:
+            # parameters are the program's last inputs: released once no launch reads them
+            self.released = [Event() for _ in self.params]
+            nin = program.num_inputs
+            program.set_input_events([None] * (nin - len(self.params)) + self.released)
 
     def step_host(self, host_inputs, stream) -> None:
         """step() with the batch in page-locked host memory (PinnedBuffer per input).
@@ -169,12 +180,19 @@ class DataParallelSGD:
         """Queues forward+backward on the local shard, the gradient all-reduce and the
         update; the local shard's loss is left in `self.loss` (device)."""
         self.program.run_device(list(batch_inputs) + self.params, [self.loss] + self.grad_ptrs, stream)
-        if self.overlap:
+        if self.overlap or self.early_update:
             for i in self.order:
                 self.ready[i].wait(self.comm_stream)
-                self.comm.allreduce_sum(self.grad_ptrs[i], self.sizes[i], self.comm_stream)
+                if self.overlap:
+                    self.comm.allreduce_sum(self.grad_ptrs[i], self.sizes[i], self.comm_stream)
+                if self.early_update:
+                    self.released[i].wait(self.comm_stream)
+                    self.opt.step_one(i, self.grad_ptrs[i], self.comm_stream, lr_scale=1.0 / self.world)
             self.exchanged.record(self.comm_stream)
             self.exchanged.wait(stream)
-        elif self.comm is not None:
+            if not self.early_update:
+                self.opt.step(self.grad_ptrs, stream, lr_scale=1.0 / self.world)
+            return
+        if self.comm is not None:
             self.comm.allreduce_sum(self.grads.ptr, sum(self.sizes), stream)
         self.opt.step(self.grad_ptrs, stream, lr_scale=1.0 / self.world)

@@ -36,6 +36,16 @@ class SGD:
         self._v = (ctypes.c_void_p * max(1, n))(*[v.ptr for v in self.velocities]) if self.velocities else None
         self._n = (ctypes.c_int64 * max(1, n))(*[p.nbytes // 4 for p in self.params])
 
+    def step_one(self, i: int, grad, stream=None, lr_scale: float = 1.0) -> None:
+        """Queues the update of parameter i alone (same arithmetic as step)."""
+        gp = (ctypes.c_void_p * 1)(getattr(grad, "ptr", grad))
+        pp = (ctypes.c_void_p * 1)(self.params[i].ptr)
+        vp = (ctypes.c_void_p * 1)(self.velocities[i].ptr) if self.velocities else None
+        nn = (ctypes.c_int64 * 1)(self.params[i].nbytes // 4)
+        h = stream.handle if isinstance(stream, Stream) else stream
+        _lib.check(_lib.lib.tt_sgd_step(1, pp, gp, vp, nn, ctypes.c_float(self.lr * lr_scale),
+                                        ctypes.c_float(self.momentum), h))
+
     def step(self, grads, stream=None, lr_scale: float = 1.0) -> None:
         """Queues the update on `stream`; lr_scale folds e.g. 1/world for data parallel."""
         if len(grads) != len(self.params):
