@@ -83,8 +83,8 @@ def test_region_output_also_read_elsewhere_keeps_fp32(cache_dir):
 
 def test_special_values_survive_the_copies(cache_dir):
     """NaN and inf in X reach the GEMM through the copies as the pre-pass would pass
-    them: a row holding NaN gives NaN, a row holding inf gives non-finite values (inf
-    or NaN: the known 3xTF32 limitation); the finite rows stay within tolerance."""
+    them: a row holding NaN gives NaN, a row holding inf gives the reference's signed
+    infinities; the finite rows stay within tolerance."""
     rng = np.random.default_rng(43)
     a, b = _data(rng, (256, 256), 1.0), np.ones((256, 256), np.float32)
     a[3, 7] = np.nan
@@ -96,6 +96,9 @@ def test_special_values_survive_the_copies(cache_dir):
     assert "(A hi/lo from [0])" in prog.execution_plan()
     got = prog.run({na: a, nb: b, ny: y}).numpy()
     assert np.all(np.isnan(got[3])) and not np.any(np.isfinite(got[9]))
+    ref9 = O.matmul(a[9:10], y)[0]
+    assert np.array_equal(np.isnan(got[9]), np.isnan(ref9)) and np.array_equal(got[9][np.isinf(ref9)],
+                                                                                   ref9[np.isinf(ref9)])
     keep = np.ones(256, bool)
     keep[[3, 9]] = False
     assert_norm(got[keep], O.matmul(a[keep], y), GEMM_FROB_RTOL)

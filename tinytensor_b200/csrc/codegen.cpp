@@ -442,16 +442,20 @@ std::string generate_source(Plan& p) {
           "  const float ex = tt_exp(x);\n"
           "  return ex / (1.0f + ex);\n"
           "}\n";
-    ss << "// hi/lo operand split of the 3xTF32 GEMM: hi = x with its low 13 mantissa bits cleared,\n"
-          "// lo = the same of x - hi (exact); NaN -> the canonical quiet NaN, +-inf -> (x, 0).\n";
+    ss << "// hi/lo operand split of the 3xTF32 GEMM (the pre-pass's split_tf32, bit for bit): hi = x\n"
+          "// with its low 13 mantissa bits cleared, lo = the same of x - hi (exact), or the sign\n"
+          "// marker hi * 2^-24 when that is zero and x is not; +-inf -> (x, x); NaN -> the\n"
+          "// canonical quiet NaN twice.  A nonzero lo keeps inf * finite products infinite.\n";
     ss << "__device__ __forceinline__ void tt_split(float x, float& hi, float& lo) {\n"
           "  const unsigned u = __float_as_uint(x);\n"
           "  if ((u & 0x7F800000u) != 0x7F800000u) {\n"
           "    hi = __uint_as_float(u & 0xFFFFE000u);\n"
-          "    lo = __uint_as_float(__float_as_uint(__fsub_rn(x, hi)) & 0xFFFFE000u);\n"
+          "    const float r = __uint_as_float(__float_as_uint(__fsub_rn(x, hi)) & 0xFFFFE000u);\n"
+          "    lo = (r == 0.0f && x != 0.0f) ? __uint_as_float(__float_as_uint(__fmul_rn(hi, 0x1p-24f)) & 0xFFFFE000u)"
+          " : r;\n"
           "  } else {\n"
           "    hi = (u & 0x7FFFFFFFu) > 0x7F800000u ? __uint_as_float(0x7FC00000u) : x;\n"
-          "    lo = 0.0f;\n"
+          "    lo = hi;\n"
           "  }\n"
           "}\n\n";
     for (Launch& L : p.launches)

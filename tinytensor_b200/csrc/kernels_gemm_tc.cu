@@ -732,16 +732,27 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
 }
 
 // ---- split pre-pass ----
-// hi = trunc_tf32(x), lo = trunc_tf32(x - hi) (x - hi is exact in fp32).  NaN becomes
-// the canonical quiet NaN, whose payload survives the truncation; for +-inf lo = 0.
+// hi = trunc_tf32(x), lo = trunc_tf32(x - hi) (x - hi is exact in fp32).
+// Non-finite products follow the reference's fp32 loop (src/core/operators.cpp:235-319),
+// where a.b is +-inf for a = +-inf and any finite nonzero b, and NaN for inf * 0.  In
+// C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi a zero lo part next to an infinite partner
+// would add an inf * 0 = NaN term, so lo is never zero for a nonzero x:
+//   - x nonzero and tf32-exact (x - hi == 0): lo = hi * 2^-24, a marker of x's sign
+//     (it moves the represented value by 2^-24 relative, below the scheme's 2^-21);
+//   - x = +-inf: hi = lo = x;  NaN: hi = lo = the canonical quiet NaN (its payload
+//     survives the truncation);  x = +-0: hi = x, lo = +0.
+// Then every product term with an infinite factor is inf of the right sign (or NaN
+// for inf * 0, as in the reference), and sums of them behave as the reference's.  The
+// marker underflows only for |x| < 2^-102 (then an inf partner gives NaN, not inf).
 __device__ __forceinline__ float trunc_tf32(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     if (isfinite(x)) {
         hi = trunc_tf32(x);
-        lo = trunc_tf32(__fsub_rn(x, hi));
+        const float r = trunc_tf32(__fsub_rn(x, hi));
+        lo = (r == 0.0f && x != 0.0f) ? trunc_tf32(__fmul_rn(hi, 0x1p-24f)) : r;
     } else {
         hi = isnan(x) ? __uint_as_float(0x7FC00000u) : x;
-        lo = 0.0f;
+        lo = hi;
     }
 }
 
