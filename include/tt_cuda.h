@@ -131,8 +131,6 @@ typedef struct tt_compile_options {
 #define TT_FLAG_SERIAL 8          /* every launch on the run's stream, one after another (by
                                      default two adjacent independent GEMMs run side by side
                                      on a second stream of the program) */
-#define TT_FLAG_NO_SIDE_PRODUCT 16 /* skinny products stay GEMM launches of their own instead of
-                                      being formed in the producing GEMM's epilogue (diagnostics) */
 
 typedef struct tt_program tt_program;
 

@@ -23,7 +23,7 @@ from ._lib import (  # noqa: F401
     TinyTensorError,
     TypeError,
 )
-from ._lib import FLAG_HOST_ONLY, FLAG_NO_FUSION, FLAG_NO_GEMM_FUSION, FLAG_NO_SIDE_PRODUCT, FLAG_SERIAL  # noqa: F401
+from ._lib import FLAG_HOST_ONLY, FLAG_NO_FUSION, FLAG_NO_GEMM_FUSION, FLAG_SERIAL  # noqa: F401
 from .compiler import (  # noqa: F401
     CompiledProgram,
     CudaGraph,

@@ -23,7 +23,7 @@ OP_EXP, OP_NEG, OP_TANH, OP_REDUCE_MAX, OP_STEP, OP_RESHAPE, OP_EXPAND = range(1
 HOST, DEVICE = 0, 1
 H2D, D2H, D2D = 1, 2, 3
 INFO_ORIGINAL_IR, INFO_OPTIMIZED_IR, INFO_SOURCE, INFO_PLAN, INFO_CUBIN_PATH = range(5)
-FLAG_NO_FUSION, FLAG_NO_GEMM_FUSION, FLAG_HOST_ONLY, FLAG_SERIAL, FLAG_NO_SIDE_PRODUCT = 1, 2, 4, 8, 16
+FLAG_NO_FUSION, FLAG_NO_GEMM_FUSION, FLAG_HOST_ONLY, FLAG_SERIAL = 1, 2, 4, 8
 
 
 class TinyTensorError(Exception):

@@ -216,7 +216,6 @@ int tt_compile(const tt_graph* cg, const tt_compile_options* opt, tt_program** o
         so.fuse = !(o.flags & TT_FLAG_NO_FUSION);
         so.gemm_epilogue = !(o.flags & TT_FLAG_NO_GEMM_FUSION);
         so.concurrent_gemms = !(o.flags & TT_FLAG_SERIAL);
-        so.side_products = !(o.flags & TT_FLAG_NO_SIDE_PRODUCT);
         p->plan = schedule(g, so);
         p->source = generate_source(p->plan);
         for (int k : p->plan.g.inputs) {

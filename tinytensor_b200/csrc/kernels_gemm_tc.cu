@@ -387,14 +387,6 @@ struct PairCfg {
     static constexpr int STAGE_BYTES = 4 * TILE;            // A_hi, A_lo, B_hi, B_lo of this CTA
     static constexpr int SMEM_BYTES = PAIR_STAGES * STAGE_BYTES + 2048;
 };
-// Side product: each epilogue warp stages 64 rows of W (SIDEQ floats each, zero-padded)
-// in an area of its own after the barriers.
-constexpr int SIDE_ROWS = 64;
-constexpr int SIDE_OFFSET = 256;  // bytes after the stage ring (the barriers take < 128)
-template <int BK, int SIDEQ>
-constexpr int pair_smem_bytes() {
-    return PairCfg<BK>::SMEM_BYTES + (SIDEQ > 0 ? EPI_WARPS * SIDE_ROWS * SIDEQ * 4 : 0);
-}
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
@@ -519,12 +511,8 @@ __device__ __forceinline__ PairUnit pair_unit(const TcParams& p, int u, uint32_t
 // SIDEQ > 0: the epilogue also forms the side product P = C.W (p.side_q <= SIDEQ columns):
 // each thread holds one row of its 128-column half tile after the activation, sums
 // C[row][c] * W[c][q] over those columns in column order (fmaf) and writes the sums to
-// slice 2*tile_n + half.  W's rows reach the warp through shared memory, 64 at a time
-// (one coalesced load per lane and row block, zero-padded to SIDEQ), and every lane
-// reads them as broadcast float4s; only __syncwarp orders the warp's own area, so a
-// warp that stops early (abort) leaves no other warp waiting.  This runs after the
-// tile's last chunk is drained, while the MMAs of the next tile proceed (the two TMEM
-// accumulators give it about two chunk times).
+// slice 2*tile_n + half.  This runs after the tile's last chunk is drained, while the
+// MMAs of the next tile proceed (the two TMEM accumulators give it about two chunk times).
 template <int BK, int SIDEQ>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
@@ -689,6 +677,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             const int row = w.m0 + q * 32 + lane;
             float* crow = p.C + static_cast<int64_t>(w.zb_all) * p.c_bstride + static_cast<int64_t>(row) * p.ldc;
             if (row < p.M) {
+                float y[SIDEQ > 0 ? SIDEQ : 1];
+#pragma unroll
+                for (int s = 0; s < (SIDEQ > 0 ? SIDEQ : 1); ++s) y[s] = 0.0f;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int col0 = w.n0 + h * 128 + j * 32;
@@ -708,47 +699,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                             for (int t = 0; t < 32; ++t)
                                 if (col0 + t < p.N) crow[col0 + t] = v[t];
                         }
-                    }
-                }
-            }
-            if constexpr (SIDEQ > 0) {
-                // every lane of the warp takes part (rows beyond M hold 0 and store nothing);
-                // columns beyond N hold 0 (zero-filled operands) and meet zero rows of W
-                float y[SIDEQ];
+                        if constexpr (SIDEQ > 0) {
 #pragma unroll
-                for (int s = 0; s < SIDEQ; ++s) y[s] = 0.0f;
-                {
-                    float* ws = reinterpret_cast<float*>(smem + STAGES * C_::STAGE_BYTES + SIDE_OFFSET) +
-                                e * (SIDE_ROWS * SIDEQ);
+                            for (int t = 0; t < 32; ++t) {
+                                if (col0 + t < p.N) {
+                                    const float* wr = p.side_w + static_cast<int64_t>(col0 + t) * p.side_wk;
 #pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        const int cbase = w.n0 + h * 128 + half * SIDE_ROWS;
-                        __syncwarp();
-#pragma unroll 4
-                        for (int i = 0; i < SIDE_ROWS * SIDEQ / 32; ++i) {
-                            const int idx = lane + 32 * i, r = idx / SIDEQ, s = idx - r * SIDEQ;
-                            const int col = cbase + r;
-                            ws[idx] = (col < p.N && s < p.side_q)
-                                          ? __ldg(p.side_w + static_cast<int64_t>(col) * p.side_wk + s)
-                                          : 0.0f;
-                        }
-                        __syncwarp();
-                        const float4* w4 = reinterpret_cast<const float4*>(ws);
-#pragma unroll
-                        for (int t = 0; t < SIDE_ROWS; ++t) {
-                            const float v = acc[half * SIDE_ROWS + t];
-#pragma unroll
-                            for (int f = 0; f < SIDEQ / 4; ++f) {
-                                const float4 wv = w4[t * (SIDEQ / 4) + f];
-                                y[4 * f] = fmaf(v, wv.x, y[4 * f]);
-                                y[4 * f + 1] = fmaf(v, wv.y, y[4 * f + 1]);
-                                y[4 * f + 2] = fmaf(v, wv.z, y[4 * f + 2]);
-                                y[4 * f + 3] = fmaf(v, wv.w, y[4 * f + 3]);
+                                    for (int s = 0; s < SIDEQ; ++s)
+                                        if (s < p.side_q) y[s] = fmaf(v[t], __ldg(wr + s), y[s]);
+                                }
                             }
                         }
                     }
                 }
-                if (row < p.M) {
+                if constexpr (SIDEQ > 0) {
                     float* dst = p.side_part + (static_cast<int64_t>((w.n0 >> 8) * 2 + h) * p.M + row) * p.side_q;
 #pragma unroll
                     for (int s = 0; s < SIDEQ; ++s)
@@ -1012,7 +976,7 @@ int launch_pair(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
     static int max_clusters = 0;
     std::call_once(once, [] {
         err = cudaFuncSetAttribute(gemm_tc_pair_kernel<BK, SIDEQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   pair_smem_bytes<BK, SIDEQ>());
+                                   PairCfg<BK>::SMEM_BYTES);
         if (err != cudaSuccess) return;
         int dev = 0, sms = 0;
         cudaGetDevice(&dev);
@@ -1020,7 +984,7 @@ int launch_pair(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(static_cast<unsigned>(sms > 1 ? sms : 2), 1, 1);
         cfg.blockDim = dim3(THREADS, 1, 1);
-        cfg.dynamicSmemBytes = pair_smem_bytes<BK, SIDEQ>();
+        cfg.dynamicSmemBytes = PairCfg<BK>::SMEM_BYTES;
         int n = 0;
         if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_pair_kernel<BK, SIDEQ>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
@@ -1032,8 +996,7 @@ int launch_pair(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
     const int clusters = p.n_units < max_clusters ? p.n_units : max_clusters;
     if (clusters <= 0) return 0;
     gemm_tc_pair_kernel<BK, SIDEQ>
-        <<<dim3(static_cast<unsigned>(2 * clusters)), THREADS, pair_smem_bytes<BK, SIDEQ>(), st>>>(ahi, alo, bhi, blo,
-                                                                                                 p);
+        <<<dim3(static_cast<unsigned>(2 * clusters)), THREADS, PairCfg<BK>::SMEM_BYTES, st>>>(ahi, alo, bhi, blo, p);
     return static_cast<int>(cudaGetLastError());
 }
 

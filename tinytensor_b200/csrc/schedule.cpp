@@ -890,7 +890,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
     // and P's own launch only adds the 2 * ceil(K/256) partial slices in slice order.  P
     // then no longer reads X from HBM (the MLP's output layer Y = H2.W3: 512 MB per 32768
     // rows).
-    if (opt.gemm_epilogue && opt.fuse && opt.side_products) {
+    if (opt.gemm_epilogue && opt.fuse) {
         for (size_t c = 0; c < p.launches.size(); ++c) {
             Launch& P = p.launches[c];
             GemmDesc& d = P.gd;

@@ -46,7 +46,6 @@ struct ScheduleOptions {
     bool fuse = true;
     bool gemm_epilogue = true;
     bool concurrent_gemms = true;
-    bool side_products = true;
 };
 
 Plan schedule(const Graph& g, const ScheduleOptions& opt);
