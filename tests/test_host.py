@@ -379,43 +379,6 @@ def test_dz_regions_write_the_gemm_operand_copies(cache_dir):
     assert "hi/lo" not in plain
 
 
-def test_output_layer_is_a_side_product_of_the_tanh_gemm(cache_dir):
-    """Y = H2 W3 (10 columns) is formed in the epilogue of the GEMM that stores H2 =
-    tanh(H1 W2): that GEMM writes 32 partial slices (two per 256-column tile) in a
-    buffer of their own, and Y's launch only adds them, so nothing reads H2 for Y.  A W
-    computed inside the graph (not an input) keeps the plain skinny GEMM, and so does
-    TT_FLAG_NO_GEMM_FUSION."""
-    g = tt.Graph()
-    x, t = g.input([4096, 1024]), g.input([4096, 10])
-    w1, w2, w3 = g.input([1024, 4096]), g.input([4096, 4096]), g.input([4096, 10])
-    d = tt.tanh(tt.relu(x @ w1) @ w2) @ w3 - t
-    loss = tt.mean(d * d)
-    plan = tt.compile_gradients(g, loss, [w1, w2, w3], cache_dir=cache_dir, flags=HOST).execution_plan()
-    lines = [line.strip() for line in plan.splitlines() if line.strip().startswith("[")]
-    prod = [i for i, line in enumerate(lines) if "(+ side product [" in line]
-    assert len(prod) == 1 and "+tanh" in lines[prod[0]], plan
-    j = int(re.search(r"\(\+ side product \[(\d+)\]\)", lines[prod[0]]).group(1))
-    assert lines[j].startswith(f"[{j}] gemm/side_product[4096x10x4096 32 slices from [{prod[0]}]]"), plan
-    size, off = (int(v) for v in re.search(r"side_slices=(\d+)@(\d+)", lines[prod[0]]).groups())
-    assert size == 32 * 4096 * 10 * 4
-    scratch = re.search(r"scratch=(\d+)@(\d+)", lines[prod[0]])
-    if scratch:
-        s_size, s_off = int(scratch.group(1)), int(scratch.group(2))
-        assert s_off + s_size <= off or off + size <= s_off
-    for line in lines[prod[0] + 1: j]:
-        for o in re.findall(r"-> arena:(\d+)", line):
-            assert not (off <= int(o) < off + size), line
-    assert not any("simt_skinny[4096x10x4096" in line and "A:K" in line for line in lines), plan
-    # W computed in the graph: the skinny GEMM stays
-    g2 = tt.Graph()
-    h2, v, w = g2.input([512, 512]), g2.input([512, 10]), g2.input([512, 512])
-    plan2 = _host_compile(g2, [tt.tanh(h2 @ w) @ (v * 2.0)], cache_dir).execution_plan()
-    assert "side product" not in plan2 and "simt_skinny" in plan2, plan2
-    plain = tt.compile_gradients(g, loss, [w1, w2, w3], cache_dir=cache_dir,
-                                 flags=HOST | tt.FLAG_NO_GEMM_FUSION).execution_plan()
-    assert "side product" not in plain
-
-
 def test_small_k_product_is_formed_inside_its_region(cache_dir):
     """The MLP's dH2 = dY W3^T (K = 10, read only by the dZ2 region) is no GEMM launch:
     the dZ2 region forms it; a small-K product that is also a graph output stays a GEMM."""

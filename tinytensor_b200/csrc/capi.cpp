@@ -383,13 +383,6 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
             };
             if (L.gd.a_presplit) copies(L.a_split_src, L.a_split_layout, io.a_hi, io.a_lo);
             if (L.gd.b_presplit) copies(L.b_split_src, L.b_split_layout, io.b_hi, io.b_lo);
-            if (L.side_for >= 0) {  // this GEMM also forms a skinny product's partial slices
-                const Launch& P = pl.launches[static_cast<size_t>(L.side_for)];
-                io.side_w = reinterpret_cast<const float*>(resolve(P.in_ref2)) + P.gd.b_off;
-                io.side_part = reinterpret_cast<float*>(resolve(L.side_ref));
-            } else if (L.side_of >= 0) {  // this skinny product only adds those slices
-                io.side_part = reinterpret_cast<float*>(resolve(pl.launches[static_cast<size_t>(L.side_of)].side_ref));
-            }
             rc = launch_gemm(L.gd, reinterpret_cast<const float*>(resolve(L.in_ref)),
                              reinterpret_cast<const float*>(resolve(L.in_ref2)),
                              reinterpret_cast<float*>(resolve(L.out_ref)), resolve(L.scratch_ref), status, st, &io);

@@ -1035,7 +1035,6 @@ const char* gemm_algo_name(int algo) {
 }
 
 int64_t gemm_scratch_bytes(const GemmDesc& d) {
-    if (d.side_slices > 0) return 0;
     if (d.algo == ALGO_TC) return gemm_tc_scratch_bytes(d);
     if ((d.algo == ALGO_SKINNY || d.algo == ALGO_SKINNY_T) && d.ksplit > 1) return d.batch * d.ksplit * d.M * d.N * 4;
     return 0;
@@ -1044,7 +1043,6 @@ int64_t gemm_scratch_bytes(const GemmDesc& d) {
 int gemm_launch_count(const GemmDesc& d) {
     if (d.M == 0 || d.N == 0 || d.batch == 0) return 0;
     if (d.K == 0) return static_cast<int>(d.batch);
-    if (d.side_slices > 0) return 1;
     if (d.algo == ALGO_TC) return gemm_tc_launch_count(d);
     if (d.algo == ALGO_SKINNY || d.algo == ALGO_SKINNY_T) return d.ksplit > 1 ? 2 : 1;
     return 1;
@@ -1063,11 +1061,6 @@ int launch_gemm(const GemmDesc& d, const float* A, const float* B, float* C, voi
             if (rc) return rc;
         }
         return 0;
-    }
-    if (d.side_slices > 0) {
-        // formed in an earlier GEMM's epilogue: add its partial slices in slice order
-        if (io == nullptr || io->side_part == nullptr || d.batch != 1) return static_cast<int>(cudaErrorInvalidValue);
-        return launch_splitk_reduce(io->side_part, C, d.M * d.N, d.side_slices, 1, d.c_sb, d.epilogue, stream);
     }
     if (d.algo == ALGO_TC) return launch_gemm_tc(d, A, B, C, scratch, status, stream, io);
     if (d.algo == ALGO_SKINNY || d.algo == ALGO_SKINNY_T) return launch_skinny(d, A, B, C, scratch, st);

@@ -85,12 +85,6 @@ struct TcParams {
     int group_m;                    // pair kernel: M-tiles per group of the unit order (see pair_unit)
     int epilogue;        // applied here only when ksplit == 1
     int* status;
-    // pair kernel, side product P = C.W: W[c][q] = side_w[c*side_wk + q] for the side_q
-    // (<= 16) columns of P; partial slice s of P at side_part + s*M*side_q
-    const float* side_w;
-    float* side_part;
-    int64_t side_wk;
-    int side_q;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -508,12 +502,7 @@ __device__ __forceinline__ PairUnit pair_unit(const TcParams& p, int u, uint32_t
 // stage ring, the TMEM chunk double buffer and every barrier phase run on counters
 // that continue across units, so the epilogue of one tile (its last drain and its
 // stores) overlaps the TMA loads and MMAs of the next.
-// SIDEQ > 0: the epilogue also forms the side product P = C.W (p.side_q <= SIDEQ columns):
-// each thread holds one row of its 128-column half tile after the activation, sums
-// C[row][c] * W[c][q] over those columns in column order (fmaf) and writes the sums to
-// slice 2*tile_n + half.  This runs after the tile's last chunk is drained, while the
-// MMAs of the next tile proceed (the two TMEM accumulators give it about two chunk times).
-template <int BK, int SIDEQ>
+template <int BK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                         const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
@@ -677,17 +666,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             const int row = w.m0 + q * 32 + lane;
             float* crow = p.C + static_cast<int64_t>(w.zb_all) * p.c_bstride + static_cast<int64_t>(row) * p.ldc;
             if (row < p.M) {
-                float y[SIDEQ > 0 ? SIDEQ : 1];
-#pragma unroll
-                for (int s = 0; s < (SIDEQ > 0 ? SIDEQ : 1); ++s) y[s] = 0.0f;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int col0 = w.n0 + h * 128 + j * 32;
                     if (col0 < p.N) {
-                        float* v = acc + j * 32;  // activated in place (this chunk of acc is not read again)
+                        float v[32];
 #pragma unroll
                         for (int t = 0; t < 32; ++t) {
-                            v[t] = gemm_epilogue(v[t], p.epilogue);
+                            v[t] = gemm_epilogue(acc[j * 32 + t], p.epilogue);
                         }
                         if (vec_ok && col0 + 32 <= p.N) {
 #pragma unroll
@@ -699,24 +685,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                             for (int t = 0; t < 32; ++t)
                                 if (col0 + t < p.N) crow[col0 + t] = v[t];
                         }
-                        if constexpr (SIDEQ > 0) {
-#pragma unroll
-                            for (int t = 0; t < 32; ++t) {
-                                if (col0 + t < p.N) {
-                                    const float* wr = p.side_w + static_cast<int64_t>(col0 + t) * p.side_wk;
-#pragma unroll
-                                    for (int s = 0; s < SIDEQ; ++s)
-                                        if (s < p.side_q) y[s] = fmaf(v[t], __ldg(wr + s), y[s]);
-                                }
-                            }
-                        }
                     }
-                }
-                if constexpr (SIDEQ > 0) {
-                    float* dst = p.side_part + (static_cast<int64_t>((w.n0 >> 8) * 2 + h) * p.M + row) * p.side_q;
-#pragma unroll
-                    for (int s = 0; s < SIDEQ; ++s)
-                        if (s < p.side_q) dst[s] = y[s];
                 }
             }
         }
@@ -968,14 +937,14 @@ int launch_main(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
 }
 
 // Persistent launch: one cluster per co-resident SM pair (at most one per work unit).
-template <int BK, int SIDEQ>
+template <int BK>
 int launch_pair(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
                 const TcParams& p, cudaStream_t st) {
     static std::once_flag once;
     static cudaError_t err = cudaSuccess;
     static int max_clusters = 0;
     std::call_once(once, [] {
-        err = cudaFuncSetAttribute(gemm_tc_pair_kernel<BK, SIDEQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        err = cudaFuncSetAttribute(gemm_tc_pair_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    PairCfg<BK>::SMEM_BYTES);
         if (err != cudaSuccess) return;
         int dev = 0, sms = 0;
@@ -986,7 +955,7 @@ int launch_pair(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
         cfg.blockDim = dim3(THREADS, 1, 1);
         cfg.dynamicSmemBytes = PairCfg<BK>::SMEM_BYTES;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_pair_kernel<BK, SIDEQ>, &cfg) != cudaSuccess || n <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_pair_kernel<BK>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = sms / 2 > 0 ? sms / 2 : 1;
         }
@@ -995,8 +964,8 @@ int launch_pair(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
     if (err != cudaSuccess) return static_cast<int>(err);
     const int clusters = p.n_units < max_clusters ? p.n_units : max_clusters;
     if (clusters <= 0) return 0;
-    gemm_tc_pair_kernel<BK, SIDEQ>
-        <<<dim3(static_cast<unsigned>(2 * clusters)), THREADS, PairCfg<BK>::SMEM_BYTES, st>>>(ahi, alo, bhi, blo, p);
+    gemm_tc_pair_kernel<BK><<<dim3(static_cast<unsigned>(2 * clusters)), THREADS, PairCfg<BK>::SMEM_BYTES, st>>>(
+        ahi, alo, bhi, blo, p);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -1103,10 +1072,6 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
     const int64_t nkb = (d.K + bk - 1) / bk;
     TcParams p;
     p.group_m = 1;
-    p.side_w = nullptr;
-    p.side_part = nullptr;
-    p.side_wk = 0;
-    p.side_q = 0;
     p.M = static_cast<int>(d.M);
     p.N = static_cast<int>(d.N);
     p.K = static_cast<int>(d.K);
@@ -1137,19 +1102,7 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
         // MLP's 4096-wide products) groups read 3-11 % fewer DRAM bytes but ran within
         // +-1 % of rows (1 % slower at K = 1024), so rows stay there.
         p.group_m = p.tiles_n > 16 ? TT_GEMM_GROUP_M : 1;
-        if (d.side_q > 0) {
-            if (io == nullptr || io->side_w == nullptr || io->side_part == nullptr || d.side_q > 16 || d.ksplit != 1 ||
-                d.batch != 1)
-                return static_cast<int>(cudaErrorInvalidValue);  // the scheduler never plans this
-            p.side_w = io->side_w;
-            p.side_part = io->side_part;
-            p.side_wk = d.side_wk;
-            p.side_q = d.side_q;
-            rc = d.side_q <= 12 ? launch_pair<32, 12>(m_ahi, m_alo, m_bhi, m_blo, p, st)
-                                : launch_pair<32, 16>(m_ahi, m_alo, m_bhi, m_blo, p, st);
-        } else {
-            rc = launch_pair<32, 0>(m_ahi, m_alo, m_bhi, m_blo, p, st);
-        }
+        rc = launch_pair<32>(m_ahi, m_alo, m_bhi, m_blo, p, st);
     } else {
         dim3 grid(static_cast<unsigned>((d.N + BN - 1) / BN), static_cast<unsigned>((d.M + BM - 1) / BM),
                   static_cast<unsigned>(d.batch * d.ksplit));

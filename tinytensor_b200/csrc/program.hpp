@@ -66,30 +66,15 @@ struct GemmDesc {
     // Tensor-core kernel only: operands whose hi/lo copies the elementwise region that
     // produced them already wrote (no pre-pass for them here).
     int a_presplit = 0, b_presplit = 0;
-    // Side product (CTA-pair tensor-core kernel, ksplit 1, no batch): a later skinny
-    // product P = C.W (W [N][side_q], side_q <= 16, rows of W contiguous) is formed in
-    // this GEMM's epilogue from the C values it stores; each CTA half tile (128 rows x
-    // 128 columns) writes the partial sums of its columns to slice 2*tile_n + half of
-    // [slices][M][side_q].
-    int side_q = 0;
-    int64_t side_wk = 0;                   // W row stride (elements; a row = one column of C)
-    // On the skinny product itself: it only adds the `side_slices` partial slices that
-    // the earlier GEMM wrote (split-K reduce), in slice order.
-    int side_slices = 0;
 };
 // Device pointers of pre-split operands' hi/lo copies (compact K-major, rows padded to
-// round4(K) floats), null for operands split by the GEMM's own pre-pass; and of a side
-// product's W and partial slices.
+// round4(K) floats), null for operands split by the GEMM's own pre-pass.
 struct GemmSplitIO {
     const float* a_hi = nullptr;
     const float* a_lo = nullptr;
     const float* b_hi = nullptr;
     const float* b_lo = nullptr;
-    const float* side_w = nullptr;
-    float* side_part = nullptr;
 };
-// Partial slices of a side product of a GEMM with N columns (2 per 256-column tile).
-inline int64_t side_slices_of(int64_t N) { return 2 * ((N + 255) / 256); }
 // Hi/lo operand copies of a row-major [R][C] matrix, one buffer: layout 0 = its own
 // layout [R][round4(C)] (hi, then lo), layout 1 = transposed [C][round4(R)] (hi, lo).
 // A GEMM reading the matrix along its rows (A = X or B = X^T) uses layout 0, one
@@ -167,10 +152,6 @@ struct Launch {
     // GEMM: for a pre-split operand, the region launch that wrote its copies and the layout read
     int a_split_src = -1, a_split_layout = 0;
     int b_split_src = -1, b_split_layout = 0;
-    // Side product: on the tensor-core GEMM, the skinny launch whose product it forms
-    // (side_ref = its partial slices); on that skinny launch, the GEMM that forms it.
-    int side_for = -1, side_of = -1;
-    BufRef side_ref;
 };
 
 struct Slot {

@@ -882,46 +882,6 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         }
     }
 
-    // ---- skinny products formed in the epilogue of the GEMM that produced their operand ----
-    // P = X.W with X [M][K] the stored output of a CTA-pair tensor-core GEMM (no split-K,
-    // no batch) read K-major, and W [K][Q] (Q <= 16, contiguous rows) a graph input: the
-    // GEMM's epilogue has X's values in registers when it stores them, so it also forms
-    // each half tile's partial sums of P (128 columns of X against the matching rows of W),
-    // and P's own launch only adds the 2 * ceil(K/256) partial slices in slice order.  P
-    // then no longer reads X from HBM (the MLP's output layer Y = H2.W3: 512 MB per 32768
-    // rows).
-    if (opt.gemm_epilogue && opt.fuse) {
-        for (size_t c = 0; c < p.launches.size(); ++c) {
-            Launch& P = p.launches[c];
-            GemmDesc& d = P.gd;
-            if (P.type != LT_GEMM || d.algo != 1 /* simt_skinny */ || d.batch != 1 || d.N > 16 || d.a_off != 0 ||
-                d.a_sk != 1 || P.in_node2 < 0 || (d.b_sn != 1 && d.N > 1))
-                continue;
-            if (g.nodes[static_cast<size_t>(P.in_node2)].op != TT_OP_INPUT) continue;  // W exists before the GEMM runs
-            for (size_t gi = 0; gi < c; ++gi) {
-                Launch& G = p.launches[gi];
-                if (G.type != LT_GEMM || G.out_node != P.in_node) continue;
-                const GemmDesc& e = G.gd;
-                if (e.algo == 2 /* tcgen05 */ && e.pair && e.ksplit == 1 && e.batch == 1 && e.side_q == 0 &&
-                    d.M == e.M && d.K == e.N && d.a_sm == e.N) {
-                    G.gd.side_q = static_cast<int>(d.N);
-                    G.gd.side_wk = d.b_sk;
-                    G.side_for = static_cast<int>(c);
-                    P.side_of = static_cast<int>(gi);
-                    d.side_slices = static_cast<int>(side_slices_of(e.N));
-                    P.scratch_bytes = 0;
-                    std::ostringstream lg, lp;
-                    lg << " (+ side product [" << c << "])";
-                    G.label += lg.str();
-                    lp << "gemm/side_product[" << d.M << "x" << d.N << "x" << d.K << " " << d.side_slices
-                       << " slices from [" << gi << "]]";
-                    P.label = lp.str();
-                }
-                break;
-            }
-        }
-    }
-
     // ---- concurrent GEMM pairs ----
     // Two adjacent tensor-core GEMM launches, the second neither reading the first's
     // output nor writing what the first reads, each of at most four waves of CTAs, run
@@ -1000,15 +960,6 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         lives.push_back(Life{-1 - nlaunch - static_cast<int>(s), plan_step[s], last,
                              split_copies_bytes(r.copy_R, r.copy_C, r.copy_rows, r.copy_t)});
     }
-    // a side product's partial slices: from the GEMM that writes them to the launch that adds them
-    for (size_t s = 0; s < p.launches.size(); ++s) {
-        const Launch& L = p.launches[s];
-        if (L.side_for < 0) continue;
-        const GemmDesc& d = p.launches[static_cast<size_t>(L.side_for)].gd;
-        lives.push_back(Life{-1 - 2 * nlaunch - static_cast<int>(s), plan_step[s],
-                             plan_step[static_cast<size_t>(L.side_for)],
-                             static_cast<int64_t>(d.side_slices) * d.M * d.N * static_cast<int64_t>(sizeof(float))});
-    }
     p.num_intermediates = lives.size();
     for (const Life& l : lives) p.total_alloc_bytes += l.bytes;
     for (size_t s = 0; s <= p.launches.size(); ++s) {
@@ -1065,8 +1016,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
         r.offset = p.slots[static_cast<size_t>(l.slot)].offset;
         if (l.root >= 0) p.root_ref[static_cast<size_t>(l.root)] = r;
         else if (-1 - l.root < nlaunch) p.launches[static_cast<size_t>(-1 - l.root)].scratch_ref = r;
-        else if (-1 - l.root < 2 * nlaunch) p.launches[static_cast<size_t>(-1 - nlaunch - l.root)].split_ref = r;
-        else p.launches[static_cast<size_t>(-1 - 2 * nlaunch - l.root)].side_ref = r;
+        else p.launches[static_cast<size_t>(-1 - nlaunch - l.root)].split_ref = r;
     }
     p.stage_in_offset = off;
     for (int k : g.inputs) {
@@ -1162,10 +1112,6 @@ std::string plan_text(const Plan& p) {
             ss << " ->" << " " << kind_name(L.out_ref.kind) << ":"
                << (L.out_ref.kind == BK_ARENA ? L.out_ref.offset : L.out_ref.index);
             if (L.scratch_bytes) ss << " scratch=" << L.scratch_bytes << "@" << L.scratch_ref.offset;
-            if (L.side_for >= 0) {
-                const GemmDesc& d = p.launches[static_cast<size_t>(L.side_for)].gd;
-                ss << " side_slices=" << static_cast<int64_t>(d.side_slices) * d.M * d.N * 4 << "@" << L.side_ref.offset;
-            }
         }
         if (L.concurrent_next) ss << "  || runs beside [" << s + 1 << "] on the second stream";
         ss << "\n";
