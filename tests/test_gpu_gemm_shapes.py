@@ -209,3 +209,37 @@ def test_skinny_batched_both_layouts(cache_dir):
     for i in range(bsz):
         _check(c1[i], a[i], b[i])
         _check(c2[i], np.ascontiguousarray(h[i].T), b[i])
+
+
+@pytest.mark.parametrize("m,n,k,batch,act", [
+    (4096, 4096, 4096, 1, None),     # 256 tiles on 74 clusters: 34 tail tiles in 2 K pieces
+    (16384, 1024, 4096, 1, "relu"),  # the rectangular config shape, ReLU applied by the tail reduce
+    (3000, 2000, 1024, 1, "tanh"),   # partial edge tiles among the tail tiles
+    (1024, 1024, 512, 5, None),      # batched: tail tiles in the last batch
+])
+def test_tail_split_tiles(m, n, k, batch, act, cache_dir):
+    """The persistent pair kernel splits the tiles of its last, part-filled round of
+    clusters along K; their pieces go through partial tiles that a reduce adds in piece
+    order.  Checked against the oracle on sampled rows (all rows of the tail tiles
+    included) and against fp64."""
+    rng = np.random.default_rng(m + n + k + batch)
+    shape_a = [batch, m, k] if batch > 1 else [m, k]
+    a, b = _data(rng, shape_a, k), _data(rng, (k, n), k)
+    g = tt.Graph()
+    na, nb = g.input(shape_a), g.input([k, n])
+    y = na @ nb
+    y = {"relu": tt.relu, "tanh": tt.tanh, None: lambda t: t}[act](y)
+    prog = tt.compile(g, outputs=[y], cache_dir=cache_dir)
+    assert " tail" in prog.execution_plan(), prog.execution_plan()
+    c = prog.run({na: a, nb: b}).numpy()
+    act_np = {"relu": lambda v: O.unary(O.RELU, v), "tanh": lambda v: O.unary(O.TANH, v), None: lambda v: v}[act]
+    if batch > 1:
+        for z in range(batch):
+            assert_norm(c[z], act_np(O.matmul(a[z], b)), GEMM_FROB_RTOL)
+        return
+    # the last rows of C hold the tail tiles (row-major tile order): check every third of them
+    rows = np.unique(np.concatenate([np.random.default_rng(9).integers(0, m, 64), np.arange(max(0, m - 600), m, 3)]))
+    ref = act_np(O.matmul_rows(a, b, rows.astype(np.int64)))
+    assert_norm(c[rows], ref, GEMM_FROB_RTOL)
+    assert_norm(c[rows], act_np((a[rows].astype(np.float64) @ b.astype(np.float64)).astype(np.float32)),
+                GEMM_FROB_RTOL)

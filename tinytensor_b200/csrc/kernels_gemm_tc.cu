@@ -83,6 +83,10 @@ struct TcParams {
     int ksplit, kb_per_split, chunk_kb;
     int tiles_m, tiles_n, n_units;  // pair kernel: 256x256 tiles and work units (tiles x batch x splits)
     int group_m;                    // pair kernel: M-tiles per group of the unit order (see pair_unit)
+    // pair kernel tail split (tail_split > 0, ksplit 1): units >= n_full are pieces of the
+    // last tiles, tail_kb K blocks each, written to tail_part[piece][256][256]
+    int n_full, tail_split, tail_kb;
+    float* tail_part;
     int epilogue;        // applied here only when ksplit == 1
     int* status;
 };
@@ -472,29 +476,59 @@ constexpr uint32_t kIdescPair = (1u << 4) | (2u << 7) | (2u << 10) | (static_cas
 // by the tiles of its row or column), and the B panels at the turn between two groups
 // are still in L2.  group_m = 1 walks rows of tiles (N-tiles fastest), alternating
 // direction.
+// Tail split (tail_split = S > 0): when the tiles leave the last round of clusters part
+// full (r = T mod clusters tiles), units [0, n_full) are whole tiles as above and units
+// n_full + v (v < r * S) are piece v % S of tile n_full + v / S: K blocks
+// [piece * tail_kb, +tail_kb), stored without activation as a partial tile
+// tail_part[v][256][256].  Each cluster of the last round then takes one piece, so that
+// round lasts about 1/S of a tile instead of a whole one; tail_reduce_kernel adds the S
+// partials of each tile in piece order and applies the activation.
 struct PairUnit {
-    int n0, m0, nb0, zb_all, za, zb, kb0, kcount;
+    int n0, m0, nb0, zb_all, za, zb, kb0, kcount, piece;
 };
+
+struct PairTile {
+    int tm, tn, zz;
+};
+
+// Tile t of the raster order described above (zz = batch, or batch * ksplit + split).
+__device__ __forceinline__ PairTile pair_tile(int tiles_m, int tiles_n, int group_m, int t) {
+    PairTile r;
+    const int per_z = tiles_m * tiles_n;
+    r.zz = t / per_z;
+    const int rem = t - r.zz * per_z;
+    const int span = group_m * tiles_n;  // units of a full group
+    const int g = rem / span, first = g * group_m;
+    const int gsz = min(group_m, tiles_m - first);
+    const int i = rem - g * span;
+    r.tm = first + i % gsz;
+    r.tn = (g & 1) ? tiles_n - 1 - i / gsz : i / gsz;
+    return r;
+}
 
 __device__ __forceinline__ PairUnit pair_unit(const TcParams& p, int u, uint32_t rank, int nkb_total) {
     PairUnit w;
-    const int per_z = p.tiles_m * p.tiles_n;
-    const int zz = u / per_z, rem = u - zz * per_z;
-    const int span = p.group_m * p.tiles_n;  // units of a full group
-    const int g = rem / span, first = g * p.group_m;
-    const int gsz = min(p.group_m, p.tiles_m - first);
-    const int i = rem - g * span;
-    const int tm = first + i % gsz;
-    const int tn = (g & 1) ? p.tiles_n - 1 - i / gsz : i / gsz;
-    w.n0 = tn * 256;
-    w.m0 = tm * 256 + static_cast<int>(rank) * 128;
+    int t = u;
+    w.piece = -1;
+    if (p.tail_split > 0 && u >= p.n_full) {
+        const int v = u - p.n_full, tile = v / p.tail_split;
+        t = p.n_full + tile;
+        w.piece = v;
+        w.kb0 = (v - tile * p.tail_split) * p.tail_kb;
+        w.kcount = max(0, min(nkb_total, w.kb0 + p.tail_kb) - w.kb0);
+    }
+    const PairTile pt = pair_tile(p.tiles_m, p.tiles_n, p.group_m, t);
+    w.n0 = pt.tn * 256;
+    w.m0 = pt.tm * 256 + static_cast<int>(rank) * 128;
     w.nb0 = w.n0 + static_cast<int>(rank) * 128;
-    w.zb_all = zz;
-    const int batch = zz / p.ksplit, split = zz - batch * p.ksplit;
+    w.zb_all = pt.zz;
+    const int batch = pt.zz / p.ksplit, split = pt.zz - batch * p.ksplit;
     w.za = p.a_batched ? batch : 0;
     w.zb = p.b_batched ? batch : 0;
-    w.kb0 = split * p.kb_per_split;
-    w.kcount = max(0, min(nkb_total, w.kb0 + p.kb_per_split) - w.kb0);
+    if (w.piece < 0) {
+        w.kb0 = split * p.kb_per_split;
+        w.kcount = max(0, min(nkb_total, w.kb0 + p.kb_per_split) - w.kb0);
+    }
     return w;
 }
 
@@ -664,7 +698,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             }
             if (!ok) break;
             const int row = w.m0 + q * 32 + lane;
-            float* crow = p.C + static_cast<int64_t>(w.zb_all) * p.c_bstride + static_cast<int64_t>(row) * p.ldc;
+            // row `row` from column w.n0 on: in C, or in this piece's partial tile
+            const bool part = w.piece >= 0;
+            float* crow = part ? p.tail_part + (static_cast<int64_t>(w.piece) * 256 + (w.m0 & 255) + q * 32 + lane) * 256
+                               : p.C + static_cast<int64_t>(w.zb_all) * p.c_bstride + static_cast<int64_t>(row) * p.ldc +
+                                     w.n0;
+            const int ep = part ? EP_NONE : p.epilogue;
             if (row < p.M) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -673,17 +712,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                         float v[32];
 #pragma unroll
                         for (int t = 0; t < 32; ++t) {
-                            v[t] = gemm_epilogue(acc[j * 32 + t], p.epilogue);
+                            v[t] = gemm_epilogue(acc[j * 32 + t], ep);
                         }
-                        if (vec_ok && col0 + 32 <= p.N) {
+                        float* dst = crow + (col0 - w.n0);
+                        if ((vec_ok || part) && col0 + 32 <= p.N) {
 #pragma unroll
                             for (int t = 0; t < 32; t += 4)
-                                *reinterpret_cast<float4*>(crow + col0 + t) =
-                                    make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
+                                *reinterpret_cast<float4*>(dst + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
                         } else {
 #pragma unroll
                             for (int t = 0; t < 32; ++t)
-                                if (col0 + t < p.N) crow[col0 + t] = v[t];
+                                if (col0 + t < p.N) dst[t] = v[t];
                         }
                     }
                 }
@@ -728,6 +767,41 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
         float v = 0.0f;
         for (int s = 0; s < ksplit; ++s) v = __fadd_rn(v, __ldg(P + (b * ksplit + s) * per + i));
         C[b * c_bstride + i] = gemm_epilogue(v, epilogue);
+    }
+}
+
+// Adds the tail_split partial tiles of each tail tile (tail_split_pairs of the pair kernel)
+// in piece order, applies the epilogue and stores the tile's in-range part of C.  Grid:
+// (16, tail tiles); a thread handles 4 consecutive columns of a row per step.
+__global__ void __launch_bounds__(256) tail_reduce_kernel(const float* __restrict__ P, float* __restrict__ C, int M,
+                                                          int N, int64_t ldc, int64_t c_bstride, int tiles_m,
+                                                          int tiles_n, int group_m, int n_full, int S, int epilogue) {
+    const int i = blockIdx.y;
+    const PairTile pt = pair_tile(tiles_m, tiles_n, group_m, n_full + i);
+    const bool vec = (ldc % 4 == 0) && (c_bstride % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+    for (int e = blockIdx.x * 256 + threadIdx.x; e < 256 * 64; e += gridDim.x * 256) {
+        const int lr = e >> 6, lc = (e & 63) * 4;
+        const int row = pt.tm * 256 + lr, col = pt.tn * 256 + lc;
+        if (row >= M || col >= N) continue;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int s = 0; s < S; ++s) {
+            const float4 x = __ldg(reinterpret_cast<const float4*>(P + ((static_cast<int64_t>(i) * S + s) * 256 + lr) * 256 + lc));
+            v.x = __fadd_rn(v.x, x.x);
+            v.y = __fadd_rn(v.y, x.y);
+            v.z = __fadd_rn(v.z, x.z);
+            v.w = __fadd_rn(v.w, x.w);
+        }
+        v.x = gemm_epilogue(v.x, epilogue);
+        v.y = gemm_epilogue(v.y, epilogue);
+        v.z = gemm_epilogue(v.z, epilogue);
+        v.w = gemm_epilogue(v.w, epilogue);
+        float* out = C + static_cast<int64_t>(pt.zz) * c_bstride + static_cast<int64_t>(row) * ldc + col;
+        if (vec && col + 4 <= N) {
+            *reinterpret_cast<float4*>(out) = v;
+        } else {
+            const float q[4] = {v.x, v.y, v.z, v.w};
+            for (int t = 0; t < 4 && col + t < N; ++t) out[t] = q[t];
+        }
     }
 }
 
@@ -936,13 +1010,13 @@ int launch_main(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
     return static_cast<int>(cudaGetLastError());
 }
 
-// Persistent launch: one cluster per co-resident SM pair (at most one per work unit).
+// Co-resident 2-CTA clusters of the pair kernel on the current device (the occupancy
+// API; half the SM count, or 74, where it cannot be asked), with the attribute error.
 template <int BK>
-int launch_pair(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
-                const TcParams& p, cudaStream_t st) {
+int pair_max_clusters(cudaError_t* attr_err) {
     static std::once_flag once;
     static cudaError_t err = cudaSuccess;
-    static int max_clusters = 0;
+    static int max_clusters = 74;
     std::call_once(once, [] {
         err = cudaFuncSetAttribute(gemm_tc_pair_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    PairCfg<BK>::SMEM_BYTES);
@@ -957,10 +1031,20 @@ int launch_pair(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
         int n = 0;
         if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_pair_kernel<BK>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
-            n = sms / 2 > 0 ? sms / 2 : 1;
+            n = sms / 2 > 0 ? sms / 2 : 74;
         }
         max_clusters = n;
     });
+    if (attr_err) *attr_err = err;
+    return max_clusters;
+}
+
+// Persistent launch: one cluster per co-resident SM pair (at most one per work unit).
+template <int BK>
+int launch_pair(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
+                const TcParams& p, cudaStream_t st) {
+    cudaError_t err = cudaSuccess;
+    const int max_clusters = pair_max_clusters<BK>(&err);
     if (err != cudaSuccess) return static_cast<int>(err);
     const int clusters = p.n_units < max_clusters ? p.n_units : max_clusters;
     if (clusters <= 0) return 0;
@@ -1022,6 +1106,33 @@ void gemm_tc_plan(GemmDesc& d) {
         }
     }
     d.ksplit = static_cast<int>(best_ks);
+    d.tail_tiles = d.tail_split = 0;
+    // Tail split of the persistent pair kernel: with T tiles on C clusters the last round
+    // holds r = T mod C tiles; splitting each of them in S = min(C / r, chunks) K pieces
+    // gives every cluster of that round one piece, so it lasts ~1/S of a tile (plus the
+    // pieces' partial tiles, written and read back once by the reduce).  Whole tiles keep
+    // the plain epilogue.  4096^3 and 16384x1024x4096 (256 tiles on 74 clusters: 3.46
+    // rounds) drop from 4 rounds to 3.5.
+    if (d.pair) {
+        const int64_t T = ((d.M + 255) / 256) * ((d.N + 255) / 256) * d.batch;
+        const int64_t C = pair_max_clusters<32>(nullptr);
+        const int64_t k = T / C, r = T - k * C;
+        const int64_t nch = (nkb + d.chunk_kb - 1) / d.chunk_kb;
+        int64_t S = r > 0 ? std::min<int64_t>(C / r, nch) : 0;
+        if (S >= 2) {
+            const int64_t per = (nkb + S - 1) / S;
+            const int64_t tail_kb = (per + d.chunk_kb - 1) / d.chunk_kb * d.chunk_kb;
+            S = (nkb + tail_kb - 1) / tail_kb;
+            double cost = static_cast<double>(k) * (static_cast<double>(nkb) + tile_overhead_kb) +
+                          static_cast<double>(tail_kb) + tile_overhead_kb;
+            cost += 2.0 * static_cast<double>(r * S) * 65536.0 * 4.0 / bytes_per_kb;  // partial tiles
+            if (S >= 2 && cost < best_cost * 0.95) {
+                d.ksplit = 1;
+                d.tail_tiles = static_cast<int>(r);
+                d.tail_split = static_cast<int>(S);
+            }
+        }
+    }
 }
 
 // Compact hi (or lo) array size of one operand, elements.
@@ -1034,6 +1145,7 @@ int64_t gemm_tc_scratch_bytes(const GemmDesc& d) {
     const int64_t b = d.b_presplit ? 0 : operand_elems(d.N, d.K, d.b_sb, d.batch);
     int64_t bytes = 2 * align256b(a * 4) + 2 * align256b(b * 4);
     if (d.ksplit > 1) bytes += align256b(d.batch * d.ksplit * d.M * d.N * 4);
+    if (d.tail_split > 0) bytes += align256b(static_cast<int64_t>(d.tail_tiles) * d.tail_split * 65536 * 4);
     return bytes;
 }
 
@@ -1052,7 +1164,7 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
     float* alo = d.a_presplit ? const_cast<float*>(io->a_lo) : reinterpret_cast<float*>(s + a_cap);
     float* bhi = d.b_presplit ? const_cast<float*>(io->b_hi) : reinterpret_cast<float*>(s + 2 * a_cap);
     float* blo = d.b_presplit ? const_cast<float*>(io->b_lo) : reinterpret_cast<float*>(s + 2 * a_cap + b_cap);
-    float* partial = reinterpret_cast<float*>(s + 2 * a_cap + 2 * b_cap);
+    float* partial = reinterpret_cast<float*>(s + 2 * a_cap + 2 * b_cap);  // split-K partials, or tail pieces
     int rc = 0;
     if (!d.a_presplit) {
         rc = launch_split(A, ahi, alo, d.M, d.K, d.a_sm, d.a_sk, d.a_sb, ap, st);
@@ -1081,6 +1193,10 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
     p.kb_per_split = static_cast<int>((nkb + d.ksplit - 1) / d.ksplit);
     p.chunk_kb = d.chunk_kb > 0 ? d.chunk_kb : 256 / bk;
     p.status = status;
+    p.n_full = 0;
+    p.tail_split = 0;
+    p.tail_kb = 0;
+    p.tail_part = nullptr;
     if (d.ksplit > 1) {
         p.C = partial;
         p.ldc = d.N;
@@ -1102,7 +1218,23 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
         // MLP's 4096-wide products) groups read 3-11 % fewer DRAM bytes but ran within
         // +-1 % of rows (1 % slower at K = 1024), so rows stay there.
         p.group_m = p.tiles_n > 16 ? TT_GEMM_GROUP_M : 1;
+        if (d.tail_split > 0) {
+            if (d.ksplit != 1) return static_cast<int>(cudaErrorInvalidValue);  // the planner never does this
+            const int T = p.n_units;
+            p.n_full = T - d.tail_tiles;
+            p.tail_split = d.tail_split;
+            p.tail_kb = static_cast<int>((nkb + d.tail_split - 1) / d.tail_split + p.chunk_kb - 1) / p.chunk_kb *
+                        p.chunk_kb;
+            p.tail_part = partial;
+            p.n_units = p.n_full + d.tail_tiles * d.tail_split;
+        }
         rc = launch_pair<32>(m_ahi, m_alo, m_bhi, m_blo, p, st);
+        if (rc == 0 && d.tail_split > 0) {
+            tail_reduce_kernel<<<dim3(16, static_cast<unsigned>(d.tail_tiles)), 256, 0, st>>>(
+                partial, C, p.M, p.N, d.N, d.c_sb, p.tiles_m, p.tiles_n, p.group_m, p.n_full, d.tail_split,
+                d.epilogue);
+            rc = static_cast<int>(cudaGetLastError());
+        }
     } else {
         dim3 grid(static_cast<unsigned>((d.N + BN - 1) / BN), static_cast<unsigned>((d.M + BM - 1) / BM),
                   static_cast<unsigned>(d.batch * d.ksplit));
@@ -1146,14 +1278,15 @@ int launch_splitk_reduce(const float* P, float* C, int64_t per, int ksplit, int6
 }
 
 int64_t gemm_tc_ctas(const GemmDesc& d) {
-    return d.algo == 2 ? ctas_of(d) * d.ksplit : 0;
+    if (d.algo != 2) return 0;
+    return ctas_of(d) * d.ksplit + (d.tail_split > 0 ? 2LL * d.tail_tiles * (d.tail_split - 1) : 0);
 }
 
 int gemm_tc_launch_count(const GemmDesc& d) {
     int n = 1;
     if (d.M && d.K && !d.a_presplit) ++n;
     if (d.N && d.K && !d.b_presplit) ++n;
-    if (d.ksplit > 1) ++n;
+    if (d.ksplit > 1 || d.tail_split > 0) ++n;
     return n;
 }
 
