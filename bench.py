@@ -42,28 +42,20 @@ def load_peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
-def launch_key(label):
-    """(kind, MxNxK) of a GEMM launch label such as
-    'gemm/tcgen05_3xtf32[32768x4096x4096 A:K B:N +tanh]', else (label, None)."""
-    if "[" not in label:
-        return label, None
-    kind, rest = label.split("[", 1)
-    return kind, rest.split()[0].rstrip("]")
-
-
 def load_traffic(label):
-    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum, one ncu
-    capture) for the launch's kind and shape, from profiles/traffic_per_launch.txt
-    (lines '<kind> <MxNxK> <bytes> <how>'), or None when that launch was not captured."""
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture,
+    scaled to the benchmarked batch) for the launch whose label, up to its first ']', is
+    listed in profiles/traffic_per_launch.txt (tab-separated lines 'label, bytes, how');
+    None when that launch was not captured."""
     p = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
-    if not os.path.exists(p):
+    if not os.path.exists(p) or "]" not in label:
         return None
-    kind, shape = launch_key(label)
+    key = label[:label.index("]") + 1]
     with open(p) as f:
         for line in f:
-            parts = line.strip().split()
-            if len(parts) >= 3 and not line.startswith("#") and parts[0] == kind and parts[1] == shape:
-                return int(float(parts[2]))
+            parts = line.rstrip("\n").split("\t")
+            if len(parts) >= 2 and not line.startswith("#") and parts[0] == key:
+                return int(float(parts[1]))
     return None
 
 
