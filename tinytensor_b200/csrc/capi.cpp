@@ -348,6 +348,7 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
             const Region& r = pl.regions[static_cast<size_t>(L.region)];
             if (r.grid > 0) {
                 std::vector<void*> vals;
+                vals.reserve(r.ext.size() + r.store_ref.size() + 4);
                 for (size_t e = 0; e < r.ext.size(); ++e) {
                     const Access& a = r.ext_access[e];
                     vals.push_back(a.imm ? nullptr : resolve(pl.root_ref[static_cast<size_t>(a.node)]));
@@ -361,8 +362,8 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
                                                ? base + split_copies_offset(r.copy_R, r.copy_C, r.copy_rows, layout, lo)
                                                : nullptr);
                 }
-                std::vector<void*> args;
-                for (void*& v : vals) args.push_back(&v);
+                std::vector<void*> args(vals.size());
+                for (size_t i = 0; i < vals.size(); ++i) args[i] = &vals[i];
                 CUresult cr = driver().launchKernel(p->region_fn[static_cast<size_t>(L.region)],
                                                     static_cast<unsigned>(r.grid), 1, 1, 256, 1, 1, 0, st,
                                                     args.data(), nullptr);
