@@ -440,9 +440,17 @@ __global__ void __launch_bounds__(128) gemm_skinny_async_kernel(
 #endif
 constexpr int SK2_RW = TT_SK2_RW, SK2_TR = 8 * SK2_RW, SK2_TK = 128, SK2_ST = 4;
 constexpr int64_t SK2_MAX_K = 8192;
+// Y block per stage: the 32 lanes' groups of 4 k x Q floats (Q 16-B chunks each), each
+// group padded to an odd number of chunks so that the lanes' float4 reads of their own
+// group hit distinct banks (a stride of an even number of chunks put lanes l and l+4 of
+// an 8-lane phase on the same banks: 2.6 M conflicts per launch at 8192 x 10 x 4096).
 template <int Q>
-constexpr int sk2_wfloats() {  // Y block per stage, padded to whole 16-B chunks
-    return (SK2_TK * Q + 3) / 4 * 4;
+constexpr int sk2_group_floats() {
+    return 4 * (Q % 2 ? Q : Q + 1);
+}
+template <int Q>
+constexpr int sk2_wfloats() {
+    return 32 * sk2_group_floats<Q>();
 }
 template <int Q>
 constexpr int sk2_smem() {
@@ -483,13 +491,15 @@ __global__ void __launch_bounds__(256, SK2_RW <= 4 ? 2 : 1) gemm_skinny_k2_kerne
             }
             cp_async16(xs + rr * TK + 4 * c, src, bytes);
         }
-        // Y rows k0 .. k0+127: 128*Q consecutive floats (zero past the K range)
+        // Y rows k0 .. k0+127: 128*Q consecutive floats (zero past the K range), chunk e
+        // to lane group e / Q at its padded place
         float* ws = xs + TR * TK;
         const int64_t wlim = (ke - k0) * Q;  // floats of this block inside the K range
-        for (int e = tid; e < WF / 4; e += 256) {
+        for (int e = tid; e < 32 * Q; e += 256) {
             const int64_t f = 4 * static_cast<int64_t>(e);
+            const int g = e / Q, c = e - g * Q;
             const int bytes = f >= wlim ? 0 : (wlim - f >= 4 ? 16 : static_cast<int>(4 * (wlim - f)));
-            cp_async16(ws + 4 * e, bytes ? Y + k0 * Q + f : Y, bytes);
+            cp_async16(ws + g * sk2_group_floats<Q>() + 4 * c, bytes ? Y + k0 * Q + f : Y, bytes);
         }
     };
 
@@ -509,8 +519,8 @@ __global__ void __launch_bounds__(256, SK2_RW <= 4 ? 2 : 1) gemm_skinny_k2_kerne
         if (t + ST - 1 < ntiles) issue(t + ST - 1);
         cp_async_commit();
         const float* xs = sk2_smem_buf + (t % ST) * STAGE;
-        // this lane's 4 k's of Y: floats 4l*Q .. 4l*Q + 4Q - 1 of the block
-        const float4* w4 = reinterpret_cast<const float4*>(xs + TR * TK + 4 * lane * Q);
+        // this lane's 4 k's of Y: its group (4Q floats of the block, at the padded place)
+        const float4* w4 = reinterpret_cast<const float4*>(xs + TR * TK + lane * sk2_group_floats<Q>());
         float w[4 * Q];
 #pragma unroll
         for (int v = 0; v < Q; ++v) {

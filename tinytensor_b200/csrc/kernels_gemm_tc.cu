@@ -877,18 +877,22 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
 // M/N-contiguous view (s_r == 1) -> K-major hi/lo[b*l_b + r*l_r + k]: the source is
 // read as a row-major [K][R] matrix (row stride s_k) in tiles of 32 K-rows x 128 R-columns,
 // one CTA per tile.  Each warp loads rows w, w+8, w+16, w+24 of the tile with a float4 of
-// columns per lane (all four loads issued before the tile is parked in shared memory,
-// pitch 132 floats: float4 stores and float4 column-chunk reads at the minimum four
-// wavefronts); then lane = K offset, and each warp splits and writes 16 of the tile's
-// columns as 128-B runs of hi and lo along K.  Tiles are numbered K first, so the CTAs
-// resident together extend the same hi/lo rows.  vec4 (R % 4 == 0, X, s_k and s_b
-// 16-B aligned) allows the float4 loads.  Only k < K is written (the rows' padding up to
-// l_r is never read).
+// columns per lane (all four loads issued before any store) and parks them TRANSPOSED in
+// shared memory, tile[r][k] with a pitch of 33 floats: lane l's four values go to rows
+// 4l..4l+3, and the lanes of octet j store their value j first, so one store instruction
+// hits 32 distinct banks.  Then lane (rs = l / 8, k4 = l % 8) of warp w takes rows
+// r = 16w + 4i + rs (i < 4) and reads k = 4k4..4k4+3 of each (banks rs + 4k4 + k - 4k4:
+// distinct), splits the four values and writes hi and lo as one float4 each: a warp's
+// store covers 4 rows x 128 B.  Tiles are numbered K first, so the CTAs resident together
+// extend the same hi/lo rows.  vec4 (R % 4 == 0, X, s_k and s_b 16-B aligned) allows the
+// float4 loads; the float4 stores need l_r % 4 == 0 (always: rows are padded to 4) and a
+// tile whose four k's are all inside K, else scalar stores.  Only k < K is written (the
+// rows' padding up to l_r is never read).
 __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ X, float* __restrict__ hi,
                                                               float* __restrict__ lo, int64_t R, int64_t K,
                                                               int64_t s_k, int64_t s_b, int64_t l_r, int64_t l_b,
                                                               int vec4) {
-    __shared__ __align__(16) float tile[32][132];
+    __shared__ float tile[128][33];
     const int64_t b = blockIdx.y;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t tiles_k = (K + 31) / 32;
@@ -910,24 +914,45 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __res
             v[i].w = (k < K && r + 3 < R) ? __ldg(src + 3) : 0.0f;
         }
     }
+    const int rot = lane >> 3;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) *reinterpret_cast<float4*>(&tile[w + 8 * i][4 * lane]) = v[i];
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int cc = (c + rot) & 3;  // selects, not an indexed array (which would live in local memory)
+            const float e = cc == 0 ? v[i].x : cc == 1 ? v[i].y : cc == 2 ? v[i].z : v[i].w;
+            tile[4 * lane + cc][w + 8 * i] = e;
+        }
+    }
     __syncthreads();
-    const int64_t k = k0 + lane;
+    const int rs = lane >> 3, k4 = lane & 7;
+    const int64_t k = k0 + 4 * k4;
+    const bool kfull = k + 3 < K;
     float* hb = hi + b * l_b;
     float* lb = lo + b * l_b;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float4 q = *reinterpret_cast<const float4*>(&tile[lane][w * 16 + 4 * j]);
-        const float qv[4] = {q.x, q.y, q.z, q.w};
+    for (int i = 0; i < 4; ++i) {
+        const int rl = 16 * w + 4 * i + rs;
+        const int64_t rr = r0 + rl;
+        if (rr >= R) continue;
+        float4 h, l;
+        split_tf32(tile[rl][4 * k4], h.x, l.x);
+        split_tf32(tile[rl][4 * k4 + 1], h.y, l.y);
+        split_tf32(tile[rl][4 * k4 + 2], h.z, l.z);
+        split_tf32(tile[rl][4 * k4 + 3], h.w, l.w);
+        float* hd = hb + rr * l_r + k;
+        float* ld = lb + rr * l_r + k;
+        if (kfull) {
+            *reinterpret_cast<float4*>(hd) = h;
+            *reinterpret_cast<float4*>(ld) = l;
+        } else {
+            const float hv[4] = {h.x, h.y, h.z, h.w}, lv[4] = {l.x, l.y, l.z, l.w};
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int64_t rr = r0 + w * 16 + 4 * j + u;
-            if (rr < R && k < K) {
-                float h, l;
-                split_tf32(qv[u], h, l);
-                hb[rr * l_r + k] = h;
-                lb[rr * l_r + k] = l;
+            for (int u = 0; u < 4; ++u) {
+                if (k + u < K) {
+                    hd[u] = hv[u];
+                    ld[u] = lv[u];
+                }
             }
         }
     }
