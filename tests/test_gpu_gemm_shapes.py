@@ -216,16 +216,14 @@ def test_skinny_batched_both_layouts(cache_dir):
     (16384, 1024, 4096, 1, "relu"),  # the rectangular config shape, ReLU applied by the tail reduce
     (3000, 2000, 1024, 1, "tanh"),   # partial edge tiles among the tail tiles
     (1024, 1024, 512, 5, None),      # batched: tail tiles in the last batch
-    (1024, 4096, 32768, 1, None),    # 64 tiles, fewer than clusters: stream-K over all clusters (the MLP's dW1)
-    (1024, 4096, 16384, 1, "tanh"),  # stream-K with runs that cross tile edges
-    (256, 256, 8192, 1, "relu"),     # one tile in 32 pieces
+    (1024, 4096, 32768, 1, None),    # 64 tiles, fewer than clusters: all tiles are tail (the MLP's dW1)
+    (256, 256, 8192, 1, "relu"),     # one tile in 32 chunks over 74 clusters: empty runs
 ])
 def test_tail_split_tiles(m, n, k, batch, act, cache_dir):
-    """The persistent pair kernel cuts the tiles of its last, part-filled round of
-    clusters along K: each into equal pieces (one per cluster of the round) or, for long
-    K with few tiles, in equal chunk runs over all clusters (stream-K).  The pieces go
-    through partial tiles that a reduce adds in K order.  Checked against the oracle on
-    sampled rows (the rows of the tail tiles included) and against fp64."""
+    """The persistent pair kernel shares the tiles of its last, part-filled round of
+    clusters out along K over all clusters (stream-K); the pieces go through partial tiles
+    that a reduce adds in K order.  Checked against the oracle on sampled rows (the rows of
+    the tail tiles included) and against fp64."""
     rng = np.random.default_rng(m + n + k + batch)
     shape_a = [batch, m, k] if batch > 1 else [m, k]
     a, b = _data(rng, shape_a, k), _data(rng, (k, n), k)
@@ -234,9 +232,7 @@ def test_tail_split_tiles(m, n, k, batch, act, cache_dir):
     y = na @ nb
     y = {"relu": tt.relu, "tanh": tt.tanh, None: lambda t: t}[act](y)
     prog = tt.compile(g, outputs=[y], cache_dir=cache_dir)
-    plan = prog.execution_plan()
-    assert (" sk-tail" in plan) == (n == 4096 and m == 1024), plan
-    assert " tail" in plan or " sk-tail" in plan, plan
+    assert " sk-tail" in prog.execution_plan(), prog.execution_plan()
     c = prog.run({na: a, nb: b}).numpy()
     act_np = {"relu": lambda v: O.unary(O.RELU, v), "tanh": lambda v: O.unary(O.TANH, v), None: lambda v: v}[act]
     if batch > 1:

@@ -85,11 +85,10 @@ struct TcParams {
     int ksplit, kb_per_split, chunk_kb;
     int tiles_m, tiles_n, n_units;  // pair kernel: 256x256 tiles and work units (tiles x batch x splits)
     int group_m;                    // pair kernel: M-tiles per group of the unit order (see pair_unit)
-    // pair kernel tail (ksplit 1): units >= n_full are pieces of the last tiles, stored as
-    // partial tiles tail_part[piece][256][256]; even split: tail_split pieces of tail_kb K
-    // blocks per tile; stream-K (tail_clusters > 0): runs of the tail_chunks 256-K chunks
-    // (tail_nch per tile)
-    int n_full, tail_split, tail_kb, tail_clusters, tail_nch;
+    // pair kernel stream-K tail (tail_clusters > 0, ksplit 1): units >= n_full are the pieces
+    // of the last tiles (tail_nch 256-K chunks each, tail_chunks in all), partial tiles in
+    // tail_part[piece][256][256]
+    int n_full, tail_clusters, tail_nch;
     int64_t tail_chunks;
     float* tail_part;
     int epilogue;        // applied here only when ksplit == 1
@@ -481,12 +480,9 @@ constexpr uint32_t kIdescPair = (1u << 4) | (2u << 7) | (2u << 10) | (static_cas
 // by the tiles of its row or column), and the B panels at the turn between two groups
 // are still in L2.  group_m = 1 walks rows of tiles (N-tiles fastest), alternating
 // direction.
-// Tail splits: when the T tiles leave the last round of the C clusters part full (r =
-// T mod C tiles), units [0, n_full = T - r) are whole tiles as above and the r tail tiles
-// are cut along K.  Even split (tail_split = S, S * r <= C): unit n_full + v is piece
-// v % S of tile v / S, tail_kb K blocks, so each cluster of the last round takes one
-// piece.  Stream-K (tail_clusters = C > 0): the tail tiles' W = r * nch chunks of 256 K
-// (tile-major) are cut into C
+// Stream-K tail (tail_clusters = C > 0): when the T tiles leave the last round of the C
+// clusters part full (r = T mod C tiles), units [0, n_full = T - r) are whole tiles as
+// above, and the r tail tiles' W = r * nch chunks of 256 K (tile-major) are cut into C
 // equal runs, run c = chunks [c W / C, (c + 1) W / C).  A run spans at most two tiles
 // (W / C <= nch), so it is at most two pieces: unit n_full + c is its first piece and
 // unit n_full + C + c its second (empty when the run ends in its first tile).  Cluster c
@@ -521,13 +517,7 @@ __device__ __forceinline__ PairUnit pair_unit(const TcParams& p, int u, uint32_t
     PairUnit w;
     int t = u;
     w.piece = -1;
-    if (p.tail_split > 0 && u >= p.n_full) {
-        const int v = u - p.n_full, tile = v / p.tail_split;
-        t = p.n_full + tile;
-        w.piece = v;
-        w.kb0 = (v - tile * p.tail_split) * p.tail_kb;
-        w.kcount = max(0, min(nkb_total, w.kb0 + p.tail_kb) - w.kb0);
-    } else if (p.tail_clusters > 0 && u >= p.n_full) {
+    if (p.tail_clusters > 0 && u >= p.n_full) {
         const int v = u - p.n_full, C = p.tail_clusters, c = v % C;
         const int64_t nch = p.tail_nch, lo = c * p.tail_chunks / C, hi = (c + 1) * p.tail_chunks / C;
         int64_t tile = lo / nch;
@@ -809,22 +799,18 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
 constexpr int kMaxTailClusters = 128;
 __global__ void __launch_bounds__(256) tail_reduce_kernel(const float* __restrict__ P, float* __restrict__ C, int M,
                                                           int N, int64_t ldc, int64_t c_bstride, int tiles_m,
-                                                          int tiles_n, int group_m, int n_full, int split,
-                                                          int clusters, int64_t nch, int64_t chunks, int epilogue) {
+                                                          int tiles_n, int group_m, int n_full, int clusters,
+                                                          int64_t nch, int64_t chunks, int epilogue) {
     __shared__ int slots[kMaxTailClusters + 1];
     __shared__ int nslots;
     const int i = blockIdx.y;
     if (threadIdx.x == 0) {
         int n = 0;
-        if (split > 0) {  // even split: the tile's pieces are consecutive
-            for (; n < split && n < kMaxTailClusters; ++n) slots[n] = i * split + n;
-        } else {
-            const int64_t t0 = static_cast<int64_t>(i) * nch, t1 = t0 + nch;
-            for (int c = 0; c < clusters && n < kMaxTailClusters; ++c) {
-                const int64_t lo = c * chunks / clusters, hi = (c + 1) * chunks / clusters;
-                if (hi <= t0 || lo >= t1 || hi <= lo) continue;
-                slots[n++] = lo / nch == i ? c : c + clusters;
-            }
+        const int64_t t0 = static_cast<int64_t>(i) * nch, t1 = t0 + nch;
+        for (int c = 0; c < clusters && n < kMaxTailClusters; ++c) {
+            const int64_t lo = c * chunks / clusters, hi = (c + 1) * chunks / clusters;
+            if (hi <= t0 || lo >= t1 || hi <= lo) continue;
+            slots[n++] = lo / nch == i ? c : c + clusters;
         }
         nslots = n;
     }
@@ -1187,52 +1173,27 @@ void gemm_tc_plan(GemmDesc& d) {
         }
     }
     d.ksplit = static_cast<int>(best_ks);
-    d.tail_tiles = d.tail_split = d.tail_clusters = 0;
-    // Tail splits of the persistent pair kernel.  With T tiles on C clusters the last round
-    // holds r = T mod C tiles.
-    //  - even split: each tail tile in S = min(C / r, chunks) K pieces, one per cluster of
-    //    the round, so it lasts ~1/S of a tile;
-    //  - stream-K: the r * nch chunks shared out evenly over all C clusters, a run of
-    //    ceil(r * nch / C) chunks each, at most two pieces per cluster.
-    // Both add the pieces' partial tiles (written, read back once by a reduce launch);
-    // stream-K also pays a second epilogue on the clusters whose run crosses a tile edge.
-    // 256 tiles (4096^3, 16384x1024x4096, the MLP's 4096-row shards) take the even split
-    // (4 rounds -> 3.5; stream-K measured 3-12 % slower there, its per-piece costs weigh
-    // on short K); the MLP's 64-tile dW1 at K = 32768 takes stream-K (128 chunk times ->
-    // ~111), at K = 4096 neither (stream-K measured 30 % slower).  A split is taken when
-    // the model prices it 2 % cheaper than the best split-K.
+    d.tail_tiles = d.tail_clusters = 0;
+    // Stream-K tail of the persistent pair kernel: with T tiles on C clusters the last round
+    // holds r = T mod C tiles; sharing their r * nch chunks out evenly over all C clusters
+    // makes that round ceil(r * nch / C) chunks long instead of a whole tile (plus the
+    // pieces' partial tiles, written and read back once by the reduce).  Whole tiles keep
+    // the plain epilogue.  256 tiles (4096^3, 16384x1024x4096, the MLP's 4096-row shards)
+    // go from 4 rounds to ~3.5; the MLP's 64-tile dW1 (one part-full round) from 128 chunk
+    // times to ~111.  Taken when the wave model prices it 2 % cheaper than the best split-K.
     if (d.pair) {
         const int64_t T = ((d.M + 255) / 256) * ((d.N + 255) / 256) * d.batch;
         const int64_t C = pair_max_clusters<32>(nullptr);
         const int64_t k = T / C, r = T - k * C;
         const int64_t nch = (nkb + d.chunk_kb - 1) / d.chunk_kb;
-        const double whole = static_cast<double>(k) * (static_cast<double>(nkb) + tile_overhead_kb);
-        const double reduce_kb = 4.0;  // the reduce launch
-        double best_tail = best_cost * 0.98;
-        int64_t S = r > 0 ? std::min<int64_t>(C / r, nch) : 0;
-        if (S >= 2) {
-            const int64_t per = (nkb + S - 1) / S;
-            const int64_t tail_kb = (per + d.chunk_kb - 1) / d.chunk_kb * d.chunk_kb;
-            S = (nkb + tail_kb - 1) / tail_kb;
-            const double cost = whole + static_cast<double>(tail_kb) + tile_overhead_kb + reduce_kb +
-                                2.0 * static_cast<double>(r * S) * 65536.0 * 4.0 / bytes_per_kb;
-            if (S >= 2 && cost < best_tail) {
-                best_tail = cost;
-                d.ksplit = 1;
-                d.tail_tiles = static_cast<int>(r);
-                d.tail_split = static_cast<int>(S);
-            }
-        }
         if (r > 0 && C >= 2 && C <= kMaxTailClusters && nch >= 2) {
             const int64_t per = (r * nch + C - 1) / C;  // chunks per cluster in the last round
-            // pieces on every cluster of the round, up to two epilogues each, partial tiles
-            // for all of them: measured ~50 K-block times of overhead for the 64-tile dW1
-            const double cost = whole + static_cast<double>(per * d.chunk_kb) + 4.0 * tile_overhead_kb + reduce_kb +
-                                4.0 * static_cast<double>(C + r) * 65536.0 * 4.0 / bytes_per_kb;
-            if (cost < best_tail) {
+            double cost = static_cast<double>(k) * (static_cast<double>(nkb) + tile_overhead_kb) +
+                          static_cast<double>(per * d.chunk_kb) + tile_overhead_kb;
+            cost += 2.0 * static_cast<double>(C + r) * 65536.0 * 4.0 / bytes_per_kb;  // partial tiles
+            if (cost < best_cost * 0.98) {
                 d.ksplit = 1;
                 d.tail_tiles = static_cast<int>(r);
-                d.tail_split = 0;
                 d.tail_clusters = static_cast<int>(C);
             }
         }
@@ -1249,8 +1210,7 @@ int64_t gemm_tc_scratch_bytes(const GemmDesc& d) {
     const int64_t b = d.b_presplit ? 0 : operand_elems(d.N, d.K, d.b_sb, d.batch);
     int64_t bytes = 2 * align256b(a * 4) + 2 * align256b(b * 4);
     if (d.ksplit > 1) bytes += align256b(d.batch * d.ksplit * d.M * d.N * 4);
-    if (d.tail_tiles > 0)  // piece slots: r * S (even split), or two per cluster (stream-K)
-        bytes += align256b((d.tail_clusters > 0 ? 2LL * d.tail_clusters : 1LL * d.tail_tiles * d.tail_split) * 65536 * 4);
+    if (d.tail_tiles > 0) bytes += align256b(2LL * d.tail_clusters * 65536 * 4);  // two piece slots per cluster
     return bytes;
 }
 
@@ -1299,8 +1259,6 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
     p.chunk_kb = d.chunk_kb > 0 ? d.chunk_kb : 256 / bk;
     p.status = status;
     p.n_full = 0;
-    p.tail_split = 0;
-    p.tail_kb = 0;
     p.tail_clusters = 0;
     p.tail_nch = 0;
     p.tail_chunks = 0;
@@ -1327,28 +1285,20 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
         // +-1 % of rows (1 % slower at K = 1024), so rows stay there.
         p.group_m = p.tiles_n > 16 ? TT_GEMM_GROUP_M : 1;
         if (d.tail_tiles > 0) {
-            const bool sk = d.tail_clusters > 0;
-            if (d.ksplit != 1 || (sk ? d.tail_clusters > kMaxTailClusters : (d.tail_split < 2 || d.tail_split > kMaxTailClusters)))
+            if (d.ksplit != 1 || d.tail_clusters < 1 || d.tail_clusters > kMaxTailClusters)
                 return static_cast<int>(cudaErrorInvalidValue);  // the planner never does this
             p.n_full = p.n_units - d.tail_tiles;
-            p.tail_part = partial;
+            p.tail_clusters = d.tail_clusters;
             p.tail_nch = static_cast<int>((nkb + p.chunk_kb - 1) / p.chunk_kb);
-            if (sk) {
-                p.tail_clusters = d.tail_clusters;
-                p.tail_chunks = static_cast<int64_t>(d.tail_tiles) * p.tail_nch;
-                p.n_units = p.n_full + 2 * d.tail_clusters;
-            } else {
-                p.tail_split = d.tail_split;
-                p.tail_kb = static_cast<int>(((nkb + d.tail_split - 1) / d.tail_split + p.chunk_kb - 1) / p.chunk_kb *
-                                             p.chunk_kb);
-                p.n_units = p.n_full + d.tail_tiles * d.tail_split;
-            }
+            p.tail_chunks = static_cast<int64_t>(d.tail_tiles) * p.tail_nch;
+            p.tail_part = partial;
+            p.n_units = p.n_full + 2 * d.tail_clusters;
         }
         rc = launch_pair<32>(m_ahi, m_alo, m_bhi, m_blo, p, st);
         if (rc == 0 && d.tail_tiles > 0) {
             tail_reduce_kernel<<<dim3(16, static_cast<unsigned>(d.tail_tiles)), 256, 0, st>>>(
-                partial, C, p.M, p.N, d.N, d.c_sb, p.tiles_m, p.tiles_n, p.group_m, p.n_full, p.tail_split,
-                p.tail_clusters, p.tail_nch, p.tail_chunks, d.epilogue);
+                partial, C, p.M, p.N, d.N, d.c_sb, p.tiles_m, p.tiles_n, p.group_m, p.n_full, p.tail_clusters,
+                p.tail_nch, p.tail_chunks, d.epilogue);
             rc = static_cast<int>(cudaGetLastError());
         }
     } else {
@@ -1395,10 +1345,7 @@ int launch_splitk_reduce(const float* P, float* C, int64_t per, int ksplit, int6
 
 int64_t gemm_tc_ctas(const GemmDesc& d) {
     if (d.algo != 2) return 0;
-    if (d.tail_tiles > 0)
-        return ctas_of(d) + 2LL * (d.tail_clusters > 0 ? d.tail_clusters - d.tail_tiles
-                                                          : 1LL * d.tail_tiles * (d.tail_split - 1));
-    return ctas_of(d) * d.ksplit;
+    return ctas_of(d) * d.ksplit + (d.tail_tiles > 0 ? 2LL * (d.tail_clusters - d.tail_tiles) : 0);
 }
 
 int gemm_tc_launch_count(const GemmDesc& d) {
