@@ -37,9 +37,7 @@
 // Split-K (ksplit > 1, when the tile grid would leave the last wave of CTAs part-empty
 // or the GPU under-filled; chosen by gemm_tc_plan's wave model): CTA z handles a contiguous
 // range of K blocks and writes a partial tile; a reduce kernel sums the partials in
-// split order (deterministic) and applies the epilogue.  Stream-K tail (pair kernel):
-// only the tiles of the last, part-filled round of clusters are shared out along K over
-// all clusters, the rest run whole (see pair_unit).
+// split order (deterministic) and applies the epilogue.
 // No TMA multicast: every CTA loads its own tiles (the kernel also runs inside
 // multi-GPU jobs).  Every mbarrier wait is bounded by a clock budget; on expiry the
 // kernel records a code in the program's status word, raises a CTA-wide abort flag
@@ -85,11 +83,9 @@ struct TcParams {
     int ksplit, kb_per_split, chunk_kb;
     int tiles_m, tiles_n, n_units;  // pair kernel: 256x256 tiles and work units (tiles x batch x splits)
     int group_m;                    // pair kernel: M-tiles per group of the unit order (see pair_unit)
-    // pair kernel stream-K tail (tail_clusters > 0, ksplit 1): units >= n_full are the pieces
-    // of the last tiles (tail_nch 256-K chunks each, tail_chunks in all), partial tiles in
-    // tail_part[piece][256][256]
-    int n_full, tail_clusters, tail_nch;
-    int64_t tail_chunks;
+    // pair kernel tail split (tail_split > 0, ksplit 1): units >= n_full are pieces of the
+    // last tiles, tail_kb K blocks each, written to tail_part[piece][256][256]
+    int n_full, tail_split, tail_kb;
     float* tail_part;
     int epilogue;        // applied here only when ksplit == 1
     int* status;
@@ -480,16 +476,13 @@ constexpr uint32_t kIdescPair = (1u << 4) | (2u << 7) | (2u << 10) | (static_cas
 // by the tiles of its row or column), and the B panels at the turn between two groups
 // are still in L2.  group_m = 1 walks rows of tiles (N-tiles fastest), alternating
 // direction.
-// Stream-K tail (tail_clusters = C > 0): when the T tiles leave the last round of the C
-// clusters part full (r = T mod C tiles), units [0, n_full = T - r) are whole tiles as
-// above, and the r tail tiles' W = r * nch chunks of 256 K (tile-major) are cut into C
-// equal runs, run c = chunks [c W / C, (c + 1) W / C).  A run spans at most two tiles
-// (W / C <= nch), so it is at most two pieces: unit n_full + c is its first piece and
-// unit n_full + C + c its second (empty when the run ends in its first tile).  Cluster c
-// meets exactly these two units after its whole tiles, so every cluster's last round is
-// the same W / C chunks long.  A piece is stored without activation as the partial tile
-// tail_part[unit - n_full]; tail_reduce_kernel adds each tile's pieces in K order and
-// applies the activation.
+// Tail split (tail_split = S > 0): when the tiles leave the last round of clusters part
+// full (r = T mod clusters tiles), units [0, n_full) are whole tiles as above and units
+// n_full + v (v < r * S) are piece v % S of tile n_full + v / S: K blocks
+// [piece * tail_kb, +tail_kb), stored without activation as a partial tile
+// tail_part[v][256][256].  Each cluster of the last round then takes one piece, so that
+// round lasts about 1/S of a tile instead of a whole one; tail_reduce_kernel adds the S
+// partials of each tile in piece order and applies the activation.
 struct PairUnit {
     int n0, m0, nb0, zb_all, za, zb, kb0, kcount, piece;
 };
@@ -517,26 +510,12 @@ __device__ __forceinline__ PairUnit pair_unit(const TcParams& p, int u, uint32_t
     PairUnit w;
     int t = u;
     w.piece = -1;
-    if (p.tail_clusters > 0 && u >= p.n_full) {
-        const int v = u - p.n_full, C = p.tail_clusters, c = v % C;
-        const int64_t nch = p.tail_nch, lo = c * p.tail_chunks / C, hi = (c + 1) * p.tail_chunks / C;
-        int64_t tile = lo / nch;
-        int64_t a = lo, b = min(hi, (tile + 1) * nch);
-        if (v >= C) {  // second piece: the rest of the run, in the next tile
-            a = (tile + 1) * nch;
-            b = max(a, hi);
-            tile += 1;
-        }
-        const int64_t r = p.tail_chunks / nch;
-        if (tile >= r) {  // an empty second piece after the last tile
-            tile = r - 1;
-            b = a;
-        }
-        t = p.n_full + static_cast<int>(tile);
+    if (p.tail_split > 0 && u >= p.n_full) {
+        const int v = u - p.n_full, tile = v / p.tail_split;
+        t = p.n_full + tile;
         w.piece = v;
-        w.kb0 = static_cast<int>((a - tile * nch) * p.chunk_kb);
-        w.kcount = max(0, min(nkb_total, static_cast<int>((b - tile * nch) * p.chunk_kb)) - w.kb0);
-        if (b <= a) w.kcount = 0;
+        w.kb0 = (v - tile * p.tail_split) * p.tail_kb;
+        w.kcount = max(0, min(nkb_total, w.kb0 + p.tail_kb) - w.kb0);
     }
     const PairTile pt = pair_tile(p.tiles_m, p.tiles_n, p.group_m, t);
     w.n0 = pt.tn * 256;
@@ -696,7 +675,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         bool ok = true;
         for (int u = cluster; u < p.n_units && ok; u += clusters) {
             const PairUnit w = pair_unit(p, u, rank, nkb_total);
-            if (w.piece >= 0 && w.kcount == 0) continue;  // an empty stream-K piece: nothing to store
             const int nchunks = (w.kcount + p.chunk_kb - 1) / p.chunk_kb;
             float acc[128];
 #pragma unroll
@@ -792,30 +770,13 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     }
 }
 
-// Adds the stream-K pieces of each tail tile of the pair kernel in K order (the clusters
-// whose chunk runs cover the tile, in cluster order; a run that started in an earlier tile
-// contributes its second piece), applies the epilogue and stores the tile's in-range part
-// of C.  Grid: (16, tail tiles); a thread handles 4 consecutive columns of a row per step.
-constexpr int kMaxTailClusters = 128;
+// Adds the tail_split partial tiles of each tail tile (tail_split_pairs of the pair kernel)
+// in piece order, applies the epilogue and stores the tile's in-range part of C.  Grid:
+// (16, tail tiles); a thread handles 4 consecutive columns of a row per step.
 __global__ void __launch_bounds__(256) tail_reduce_kernel(const float* __restrict__ P, float* __restrict__ C, int M,
                                                           int N, int64_t ldc, int64_t c_bstride, int tiles_m,
-                                                          int tiles_n, int group_m, int n_full, int clusters,
-                                                          int64_t nch, int64_t chunks, int epilogue) {
-    __shared__ int slots[kMaxTailClusters + 1];
-    __shared__ int nslots;
+                                                          int tiles_n, int group_m, int n_full, int S, int epilogue) {
     const int i = blockIdx.y;
-    if (threadIdx.x == 0) {
-        int n = 0;
-        const int64_t t0 = static_cast<int64_t>(i) * nch, t1 = t0 + nch;
-        for (int c = 0; c < clusters && n < kMaxTailClusters; ++c) {
-            const int64_t lo = c * chunks / clusters, hi = (c + 1) * chunks / clusters;
-            if (hi <= t0 || lo >= t1 || hi <= lo) continue;
-            slots[n++] = lo / nch == i ? c : c + clusters;
-        }
-        nslots = n;
-    }
-    __syncthreads();
-    const int S = nslots;
     const PairTile pt = pair_tile(tiles_m, tiles_n, group_m, n_full + i);
     const bool vec = (ldc % 4 == 0) && (c_bstride % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
     for (int e = blockIdx.x * 256 + threadIdx.x; e < 256 * 64; e += gridDim.x * 256) {
@@ -824,8 +785,7 @@ __global__ void __launch_bounds__(256) tail_reduce_kernel(const float* __restric
         if (row >= M || col >= N) continue;
         float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         for (int s = 0; s < S; ++s) {
-            const float4 x =
-                __ldg(reinterpret_cast<const float4*>(P + (static_cast<int64_t>(slots[s]) * 256 + lr) * 256 + lc));
+            const float4 x = __ldg(reinterpret_cast<const float4*>(P + ((static_cast<int64_t>(i) * S + s) * 256 + lr) * 256 + lc));
             v.x = __fadd_rn(v.x, x.x);
             v.y = __fadd_rn(v.y, x.y);
             v.z = __fadd_rn(v.z, x.z);
@@ -840,9 +800,7 @@ __global__ void __launch_bounds__(256) tail_reduce_kernel(const float* __restric
             *reinterpret_cast<float4*>(out) = v;
         } else {
             const float q[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int t = 0; t < 4; ++t)
-                if (col + t < N) out[t] = q[t];
+            for (int t = 0; t < 4 && col + t < N; ++t) out[t] = q[t];
         }
     }
 }
@@ -1173,28 +1131,30 @@ void gemm_tc_plan(GemmDesc& d) {
         }
     }
     d.ksplit = static_cast<int>(best_ks);
-    d.tail_tiles = d.tail_clusters = 0;
-    // Stream-K tail of the persistent pair kernel: with T tiles on C clusters the last round
-    // holds r = T mod C tiles; sharing their r * nch chunks out evenly over all C clusters
-    // makes that round ceil(r * nch / C) chunks long instead of a whole tile (plus the
+    d.tail_tiles = d.tail_split = 0;
+    // Tail split of the persistent pair kernel: with T tiles on C clusters the last round
+    // holds r = T mod C tiles; splitting each of them in S = min(C / r, chunks) K pieces
+    // gives every cluster of that round one piece, so it lasts ~1/S of a tile (plus the
     // pieces' partial tiles, written and read back once by the reduce).  Whole tiles keep
-    // the plain epilogue.  256 tiles (4096^3, 16384x1024x4096, the MLP's 4096-row shards)
-    // go from 4 rounds to ~3.5; the MLP's 64-tile dW1 (one part-full round) from 128 chunk
-    // times to ~111.  Taken when the wave model prices it 2 % cheaper than the best split-K.
+    // the plain epilogue.  4096^3 and 16384x1024x4096 (256 tiles on 74 clusters: 3.46
+    // rounds) drop from 4 rounds to 3.5.
     if (d.pair) {
         const int64_t T = ((d.M + 255) / 256) * ((d.N + 255) / 256) * d.batch;
         const int64_t C = pair_max_clusters<32>(nullptr);
         const int64_t k = T / C, r = T - k * C;
         const int64_t nch = (nkb + d.chunk_kb - 1) / d.chunk_kb;
-        if (r > 0 && C >= 2 && C <= kMaxTailClusters && nch >= 2) {
-            const int64_t per = (r * nch + C - 1) / C;  // chunks per cluster in the last round
+        int64_t S = r > 0 ? std::min<int64_t>(C / r, nch) : 0;
+        if (S >= 2) {
+            const int64_t per = (nkb + S - 1) / S;
+            const int64_t tail_kb = (per + d.chunk_kb - 1) / d.chunk_kb * d.chunk_kb;
+            S = (nkb + tail_kb - 1) / tail_kb;
             double cost = static_cast<double>(k) * (static_cast<double>(nkb) + tile_overhead_kb) +
-                          static_cast<double>(per * d.chunk_kb) + tile_overhead_kb;
-            cost += 2.0 * static_cast<double>(C + r) * 65536.0 * 4.0 / bytes_per_kb;  // partial tiles
-            if (cost < best_cost * 0.98) {
+                          static_cast<double>(tail_kb) + tile_overhead_kb;
+            cost += 2.0 * static_cast<double>(r * S) * 65536.0 * 4.0 / bytes_per_kb;  // partial tiles
+            if (S >= 2 && cost < best_cost * 0.95) {
                 d.ksplit = 1;
                 d.tail_tiles = static_cast<int>(r);
-                d.tail_clusters = static_cast<int>(C);
+                d.tail_split = static_cast<int>(S);
             }
         }
     }
@@ -1210,7 +1170,7 @@ int64_t gemm_tc_scratch_bytes(const GemmDesc& d) {
     const int64_t b = d.b_presplit ? 0 : operand_elems(d.N, d.K, d.b_sb, d.batch);
     int64_t bytes = 2 * align256b(a * 4) + 2 * align256b(b * 4);
     if (d.ksplit > 1) bytes += align256b(d.batch * d.ksplit * d.M * d.N * 4);
-    if (d.tail_tiles > 0) bytes += align256b(2LL * d.tail_clusters * 65536 * 4);  // two piece slots per cluster
+    if (d.tail_split > 0) bytes += align256b(static_cast<int64_t>(d.tail_tiles) * d.tail_split * 65536 * 4);
     return bytes;
 }
 
@@ -1259,9 +1219,8 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
     p.chunk_kb = d.chunk_kb > 0 ? d.chunk_kb : 256 / bk;
     p.status = status;
     p.n_full = 0;
-    p.tail_clusters = 0;
-    p.tail_nch = 0;
-    p.tail_chunks = 0;
+    p.tail_split = 0;
+    p.tail_kb = 0;
     p.tail_part = nullptr;
     if (d.ksplit > 1) {
         p.C = partial;
@@ -1284,21 +1243,21 @@ int launch_gemm_tc(const GemmDesc& d, const float* A, const float* B, float* C, 
         // MLP's 4096-wide products) groups read 3-11 % fewer DRAM bytes but ran within
         // +-1 % of rows (1 % slower at K = 1024), so rows stay there.
         p.group_m = p.tiles_n > 16 ? TT_GEMM_GROUP_M : 1;
-        if (d.tail_tiles > 0) {
-            if (d.ksplit != 1 || d.tail_clusters < 1 || d.tail_clusters > kMaxTailClusters)
-                return static_cast<int>(cudaErrorInvalidValue);  // the planner never does this
-            p.n_full = p.n_units - d.tail_tiles;
-            p.tail_clusters = d.tail_clusters;
-            p.tail_nch = static_cast<int>((nkb + p.chunk_kb - 1) / p.chunk_kb);
-            p.tail_chunks = static_cast<int64_t>(d.tail_tiles) * p.tail_nch;
+        if (d.tail_split > 0) {
+            if (d.ksplit != 1) return static_cast<int>(cudaErrorInvalidValue);  // the planner never does this
+            const int T = p.n_units;
+            p.n_full = T - d.tail_tiles;
+            p.tail_split = d.tail_split;
+            p.tail_kb = static_cast<int>((nkb + d.tail_split - 1) / d.tail_split + p.chunk_kb - 1) / p.chunk_kb *
+                        p.chunk_kb;
             p.tail_part = partial;
-            p.n_units = p.n_full + 2 * d.tail_clusters;
+            p.n_units = p.n_full + d.tail_tiles * d.tail_split;
         }
         rc = launch_pair<32>(m_ahi, m_alo, m_bhi, m_blo, p, st);
-        if (rc == 0 && d.tail_tiles > 0) {
+        if (rc == 0 && d.tail_split > 0) {
             tail_reduce_kernel<<<dim3(16, static_cast<unsigned>(d.tail_tiles)), 256, 0, st>>>(
-                partial, C, p.M, p.N, d.N, d.c_sb, p.tiles_m, p.tiles_n, p.group_m, p.n_full, p.tail_clusters,
-                p.tail_nch, p.tail_chunks, d.epilogue);
+                partial, C, p.M, p.N, d.N, d.c_sb, p.tiles_m, p.tiles_n, p.group_m, p.n_full, d.tail_split,
+                d.epilogue);
             rc = static_cast<int>(cudaGetLastError());
         }
     } else {
@@ -1345,14 +1304,14 @@ int launch_splitk_reduce(const float* P, float* C, int64_t per, int ksplit, int6
 
 int64_t gemm_tc_ctas(const GemmDesc& d) {
     if (d.algo != 2) return 0;
-    return ctas_of(d) * d.ksplit + (d.tail_tiles > 0 ? 2LL * (d.tail_clusters - d.tail_tiles) : 0);
+    return ctas_of(d) * d.ksplit + (d.tail_split > 0 ? 2LL * d.tail_tiles * (d.tail_split - 1) : 0);
 }
 
 int gemm_tc_launch_count(const GemmDesc& d) {
     int n = 1;
     if (d.M && d.K && !d.a_presplit) ++n;
     if (d.N && d.K && !d.b_presplit) ++n;
-    if (d.ksplit > 1 || d.tail_tiles > 0) ++n;
+    if (d.ksplit > 1 || d.tail_split > 0) ++n;
     return n;
 }
 

@@ -64,10 +64,9 @@ struct GemmDesc {
     int bk = 32;                           // tensor-core kernel: K per pipeline stage (16 or 32)
     int pair = 0;                          // tensor-core kernel: 2-CTA (cta_group::2) 256x256 tiles
     // Pair kernel, ksplit 1: the last `tail_tiles` tiles (those of a last, part-filled round
-    // of clusters) are shared out along K over all `tail_clusters` clusters in equal runs of
-    // 256-K chunks (stream-K); the pieces go to partial tiles that a reduce adds in K order.
-    // tail_tiles = 0: no tail split.
-    int tail_tiles = 0, tail_clusters = 0;
+    // of clusters) are split along K in `tail_split` pieces, one per cluster; the pieces go
+    // to partial tiles that a reduce adds in piece order.  0 = no tail split.
+    int tail_tiles = 0, tail_split = 0;
     // Tensor-core kernel only: operands whose hi/lo copies the elementwise region that
     // produced them already wrote (no pre-pass for them here).
     int a_presplit = 0, b_presplit = 0;

@@ -785,7 +785,7 @@ Plan schedule(const Graph& gin, const ScheduleOptions& opt) {
             lb << "gemm/" << gemm_algo_name(d.algo) << "[" << d.M << "x" << d.N << "x" << d.K;
             if (d.batch > 1) lb << " b" << d.batch;
             if (d.ksplit > 1) lb << " splitk" << d.ksplit;
-            if (d.tail_tiles > 0) lb << " sk-tail" << d.tail_tiles;
+            if (d.tail_split > 0) lb << " tail" << d.tail_tiles << "x" << d.tail_split;
             lb << (d.a_sk == 1 ? " A:K" : " A:M") << (d.b_sn == 1 ? " B:N" : " B:K");
             if (d.epilogue != EP_NONE) lb << (d.epilogue == EP_RELU ? " +relu" : " +tanh");
             lb << "]";
