@@ -216,6 +216,7 @@ def test_skinny_batched_both_layouts(cache_dir):
     (16384, 1024, 4096, 1, "relu"),  # the rectangular config shape, ReLU applied by the tail reduce
     (3000, 2000, 1024, 1, "tanh"),   # partial edge tiles among the tail tiles
     (1024, 1024, 512, 5, None),      # batched: tail tiles in the last batch
+    (256, 256, 8192, 1, "relu"),     # a single tile in 32 K pieces
 ])
 def test_tail_split_tiles(m, n, k, batch, act, cache_dir):
     """The persistent pair kernel splits the tiles of its last, part-filled round of
