@@ -71,7 +71,7 @@ def _c(seed=3):
     return g, feed, outs
 
 
-@case("config1_chain_small", ref_ok=False)
+@case("fused_chain_small", ref_ok=False)
 def _c(seed=0):
     # the fused chain relu(a*b + c)*0.5 - exp(-a) at a small shape
     rng = np.random.default_rng(seed)
@@ -195,7 +195,7 @@ def _c(seed=12):
 
 @case("grad_mse_tanh", kind="grad", ref_ok=False)
 def _c(seed=13):
-    # the BASELINE MLP structure at a small size: relu, tanh, linear, MSE
+    # the benchmark MLP's structure at a small size: relu, tanh, linear, MSE
     rng = np.random.default_rng(seed)
     g = tt.Graph()
     x, t = g.input([32, 24]), g.input([32, 5])

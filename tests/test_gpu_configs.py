@@ -14,7 +14,7 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 
-def test_config1_fused_elementwise_1024(cache_dir):
+def test_fused_chain_1024x1024(cache_dir):
     rng = np.random.default_rng(0)
     a = rng.standard_normal((1024, 1024)).astype(np.float32)
     b = rng.standard_normal((1024, 1024)).astype(np.float32)
@@ -37,7 +37,7 @@ def test_config1_fused_elementwise_1024(cache_dir):
     assert_bitexact(got2, O.evaluate(g2, {ma: a, mb: b, mc: c}, [y2])[0])
 
 
-def test_config2_reductions_8192x4096(cache_dir):
+def test_row_reductions_8192x4096(cache_dir):
     rng = np.random.default_rng(1)
     x = rng.uniform(-1, 1, (8192, 4096)).astype(np.float32)
     g = tt.Graph()
@@ -99,19 +99,19 @@ def _gemm(m, n, k, cache_dir, rows=None):
         assert_norm(c[idx], exact, GEMM_FROB_RTOL)
 
 
-def test_config3_gemm_1024(cache_dir):
+def test_gemm_1024_cubed(cache_dir):
     _gemm(1024, 1024, 1024, cache_dir)
 
 
-def test_config3_gemm_4096_sampled(cache_dir):
+def test_gemm_4096_cubed_sampled(cache_dir):
     _gemm(4096, 4096, 4096, cache_dir, rows=48)
 
 
-def test_config3_gemm_rect_sampled(cache_dir):
+def test_gemm_16384x1024x4096_sampled(cache_dir):
     _gemm(16384, 1024, 4096, cache_dir, rows=64)
 
 
-def test_config3_gemm_8192_sampled(cache_dir):
+def test_gemm_8192_cubed_sampled(cache_dir):
     _gemm(8192, 8192, 8192, cache_dir, rows=24)
 
 
@@ -147,7 +147,7 @@ def _xavier(rng, fi, fo):
     return rng.uniform(-lim, lim, (fi, fo)).astype(np.float32)
 
 
-def test_config4_mlp_gradients_small_batch(cache_dir):
+def test_mlp_gradients_small_batch(cache_dir):
     """Full layer widths (1024 -> 4096 -> 4096 -> 10) at batch 64 against the oracle."""
     B = 64
     rng = np.random.default_rng(3)
@@ -192,8 +192,8 @@ def _fp64_mlp(x, t, w, cols):
     return out
 
 
-def test_config4_mlp_full_batch_gradients(cache_dir):
-    """Batch 4096 (the config's size): loss, dW3 in full and sampled columns of dW2 and
+def test_mlp_gradients_batch_4096(cache_dir):
+    """Batch 4096 (the single-GPU MLP benchmark's size): loss, dW3 in full and sampled columns of dW2 and
     dW1 against an fp64 recomputation, relative Frobenius <= 1e-5."""
     B = 4096
     rng = np.random.default_rng(3)
@@ -211,7 +211,7 @@ def test_config4_mlp_full_batch_gradients(cache_dir):
     assert_norm(out[1][:, cols], gw1, GEMM_FROB_RTOL)
 
 
-def test_config5_dp_step_full_global_batch_one_gpu(cache_dir):
+def test_dp_step_global_batch_32768_one_gpu(cache_dir):
     """One DataParallelSGD step at the benchmark's global batch 32768 on one GPU (the
     program, the single all-reduce-free update with lr 0.01): the gradients it used
     against fp64 (dW3 in full, sampled columns of dW2 and dW1, relative Frobenius
@@ -244,7 +244,7 @@ def test_config5_dp_step_full_global_batch_one_gpu(cache_dir):
         assert_bitexact(d.numpy(), (w0 - np.float32(0.01) * gg).astype(np.float32))
 
 
-def test_config5_sgd_steps_match_oracle(cache_dir):
+def test_mlp_sgd_steps_match_oracle(cache_dir):
     """Three SGD steps (lr 0.01) of the MLP on device vs the oracle's full-batch steps."""
     B = 32
     rng = np.random.default_rng(4)

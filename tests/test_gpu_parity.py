@@ -76,7 +76,7 @@ def test_case_matches_reference_and_oracle(name, cache_dir):
     _check(name, got, gold, orc, g)
 
 
-@pytest.mark.parametrize("name", ["add_shapes", "reductions", "matmul_shapes", "config1_chain_small"])
+@pytest.mark.parametrize("name", ["add_shapes", "reductions", "matmul_shapes", "fused_chain_small"])
 def test_device_mode_equals_host_mode(name, cache_dir):
     c = build(name)
     g, feed, outs = c["graph"], c["feed"], c["outputs"]

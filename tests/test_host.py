@@ -71,7 +71,7 @@ def test_every_case_generates_and_compiles(name, cache_dir):
             assert f.read(4) == b"\x7fELF"
 
 
-def test_config1_is_one_fused_kernel(cache_dir):
+def test_fused_chain_is_one_kernel(cache_dir):
     g = tt.Graph()
     a, b, c = g.input([1024, 1024]), g.input([1024, 1024]), g.input([1, 1024])
     y = tt.relu(a * b + c) * 0.5 - tt.exp(-a)
