@@ -217,6 +217,7 @@ def test_skinny_batched_both_layouts(cache_dir):
     (3000, 2000, 1024, 1, "tanh"),   # partial edge tiles among the tail tiles
     (1024, 1024, 512, 5, None),      # batched: tail tiles in the last batch
     (256, 256, 8192, 1, "relu"),     # a single tile in 32 K pieces
+    (4096, 4096, 2050, 1, None),     # K not a multiple of 4 or of the pieces: uneven last piece
 ])
 def test_tail_split_tiles(m, n, k, batch, act, cache_dir):
     """The persistent pair kernel splits the tiles of its last, part-filled round of
