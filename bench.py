@@ -100,6 +100,30 @@ def mlp_graph(tt, rows):
     return g, (X, T, W1, W2, W3), loss
 
 
+def bind_to_gpu_numa_node(torch, device):
+    """Restricts this process to the CPUs of the NUMA node that GPU `device` hangs off
+    (sysfs), before any page-locked host buffer is allocated, so that the per-step
+    host-to-device copies of the end-to-end loop read node-local memory when several
+    ranks copy at once.  Returns the node, or None where the topology is not exposed."""
+    try:
+        p = torch.cuda.get_device_properties(device)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            node = int(f.read().strip())
+        if node < 0:
+            return None
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            cpus = set()
+            for part in f.read().strip().split(","):
+                lo, _, hi = part.partition("-")
+                cpus.update(range(int(lo), int(hi or lo) + 1))
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return node
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
 
@@ -165,6 +189,7 @@ def run_b200(args):
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torch.distributed.run")
     torch.cuda.set_device(local)
+    numa_node = bind_to_gpu_numa_node(torch, local)
     tt.device_init(local)
     dist = None
     if world > 1:
@@ -316,6 +341,7 @@ def run_b200(args):
         "roofline": roofline,
         "step_profile": step_profile,
         "clocks": clk,
+        "host_numa_node": numa_node,
     }
     if world == 1 and not args.no_components:
         out["components"] = components(tt, torch, args, peaks, peak_src)
