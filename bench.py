@@ -120,7 +120,7 @@ def bind_to_gpu_numa_node(torch, device):
         if cpus:
             os.sched_setaffinity(0, cpus)
         return node
-    except (OSError, ValueError, AttributeError):
+    except (OSError, ValueError, AttributeError, RuntimeError):
         return None
 
 
