@@ -770,8 +770,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     }
 }
 
-// Adds the tail_split partial tiles of each tail tile (tail_split_pairs of the pair kernel)
-// in piece order, applies the epilogue and stores the tile's in-range part of C.  Grid:
+// Adds the S partial tiles of each tail tile of the pair kernel (its tail split) in piece
+// order, applies the epilogue and stores the tile's in-range part of C.  Grid:
 // (16, tail tiles); a thread handles 4 consecutive columns of a row per step.
 __global__ void __launch_bounds__(256) tail_reduce_kernel(const float* __restrict__ P, float* __restrict__ C, int M,
                                                           int N, int64_t ldc, int64_t c_bstride, int tiles_m,
