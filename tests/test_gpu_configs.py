@@ -6,7 +6,7 @@ reference's blocked loop computes independently of the other rows."""
 import numpy as np
 import pytest
 
-from parity import GEMM_FROB_RTOL, REDUCTION_NORM_RTOL, assert_bitexact, assert_elementwise_scaled, assert_norm
+from parity import GEMM_FROB_RTOL, REDUCTION_NORM_RTOL, assert_bitexact, assert_elementwise_scaled, assert_norm, norm_rel
 
 import tinytensor_b200 as tt
 from oracle import oracle as O
@@ -268,3 +268,30 @@ def test_mlp_sgd_steps_match_oracle(cache_dir):
         ref = [O.sgd(w, gw, 0.01)[0] for w, gw in zip(ref, grads)]
     for d, r in zip(dw, ref):
         assert_norm(d.numpy(), r, GEMM_FROB_RTOL)
+
+
+def test_reductions_against_both_reference_paths(cache_dir):
+    """The reference has two CPU paths for reductions: the interpreter accumulates in
+    double (src/core/operators.cpp:394-516), its compiled AVX2 code in float, one
+    sequential += per element (src/codegen/cpp_backend.cpp:389-478).  The GPU result
+    (double accumulation) is held to the interpreter at the reduction tolerance, and its
+    distance to the compiled path is reported and bounded by that path's own distance to
+    the interpreter plus the tolerance.  The reference itself (oracle/_ref) runs both."""
+    if not O.reference_available():
+        pytest.skip("oracle/_ref not built")
+    R = O.Reference()
+    rng = np.random.default_rng(1)
+    x = rng.uniform(-1, 1, (2048, 4096)).astype(np.float32)
+    g = tt.Graph()
+    nx = g.input([2048, 4096])
+    outs = [tt.sum(nx, [1]), tt.mean(nx, [1]), tt.sum(tt.transpose(nx, 0, 1), [0])]
+    got = [t.numpy() for t in tt.compile(g, outputs=outs, cache_dir=cache_dir).run({nx: x})]
+    interp = R.run(g, {nx: x}, mode="interpreted", optimize=False, outputs=outs)
+    avx2 = R.run(g, {nx: x}, mode="avx2", optimize=False, outputs=outs)
+    for name, gv, ri, ra in zip(["sum", "mean", "sum of the transpose"], got, interp, avx2):
+        assert_norm(gv, ri, REDUCTION_NORM_RTOL)
+        e_ref = norm_rel(ra, ri)     # the compiled path's own fp32 accumulation error
+        e_gpu = norm_rel(gv, ra)
+        print(f"{name}: |gpu - interpreter| {norm_rel(gv, ri):.2e}, |gpu - avx2| {e_gpu:.2e}, "
+              f"|avx2 - interpreter| {e_ref:.2e}")
+        assert e_gpu <= e_ref + REDUCTION_NORM_RTOL
