@@ -347,6 +347,11 @@ def run_b200(args):
         out["components"] = components(tt, torch, args, peaks, peak_src)
     if rank == 0 and not args.no_cpu_baseline and world == 1 and batch == GLOBAL_BATCH:
         out["cpu_baseline"] = cpu_baseline(batch)
+        if not args.no_components:
+            try:
+                out["cpu_baseline"]["components"] = cpu_components(tt)
+            except (RuntimeError, OSError, ValueError) as e:  # reported, not fatal: the headline baseline stands
+                out["cpu_baseline"]["components"] = {"unavailable": str(e)[:200]}
     if dist is not None:
         dist.barrier()
         comm.close()
@@ -502,6 +507,39 @@ def cpu_baseline(batch):
     finally:
         runner.close()
     return info
+
+
+def cpu_components(tt):
+    """The reference's compiled AVX2 code (oracle/_ref, the reference built from its
+    sources; single-threaded as shipped, one host core) on the single-GPU component
+    workloads, seconds per Executor::run with the JIT compile excluded: the CPU numbers
+    beside `components`."""
+    from oracle import oracle as O
+    if not O.reference_available():
+        return {"unavailable": "oracle/_ref/libttref.so not built"}
+    R = O.Reference()
+    rng = np.random.default_rng(0)
+    res = {"kind": "reference", "cores": 1, "mode": "compiled avx2 (avx2_fma for the GEMM), optimize=False"}
+    g = tt.Graph()  # the fused chain at [1024, 1024] with sigmoid(a) for exp(-a): the reference has no exp
+    a, b, c = g.input([1024, 1024]), g.input([1024, 1024]), g.input([1, 1024])
+    g.mark_output(tt.relu(a * b + c) * 0.5 - tt.sigmoid(a))
+    feed = {a: rng.standard_normal((1024, 1024)).astype(np.float32),
+            b: rng.standard_normal((1024, 1024)).astype(np.float32), c: rng.standard_normal((1, 1024)).astype(np.float32)}
+    t = R.time_runs(g, feed, mode="avx2", reps=5)
+    res["fused_elementwise_1024x1024_sigmoid"] = {"ms": round(t * 1e3, 3), "GB/s": round((3 * 1024 * 1024 * 4 + 4096) / t / 1e9, 2)}
+    g = tt.Graph()  # sum over axis 1 of [8192, 4096]
+    x = g.input([8192, 4096])
+    g.mark_output(tt.sum(x, [1]))
+    t = R.time_runs(g, {x: rng.uniform(-1, 1, (8192, 4096)).astype(np.float32)}, mode="avx2", reps=3)
+    res["reduce_sum_ax1_8192x4096"] = {"ms": round(t * 1e3, 2), "GB/s": round((8192 * 4096 * 4 + 8192 * 4) / t / 1e9, 2)}
+    g = tt.Graph()  # GEMM 1024^3
+    a, b = g.input([1024, 1024]), g.input([1024, 1024])
+    g.mark_output(a @ b)
+    feed = {a: rng.standard_normal((1024, 1024)).astype(np.float32),
+            b: rng.standard_normal((1024, 1024)).astype(np.float32)}
+    t = R.time_runs(g, feed, mode="avx2_fma", reps=3)
+    res["gemm_1024x1024x1024"] = {"ms": round(t * 1e3, 1), "TFLOP/s": round(2 * 1024 ** 3 / t / 1e12, 4)}
+    return res
 
 
 # Timed full reference steps stop once this much wall time is spent (at least one step),
