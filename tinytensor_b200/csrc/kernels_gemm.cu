@@ -475,11 +475,37 @@ __global__ void __launch_bounds__(256, SK2_RW <= 4 ? 2 : 1) gemm_skinny_k2_kerne
     C += static_cast<int64_t>(blockIdx.y) * c_sb;
     const int ntiles = ke > kb ? static_cast<int>((ke - kb + TK - 1) / TK) : 0;
 
+    // This thread's copy plan, fixed over the K range: X chunk i of a stage is row
+    // tid/32 + 8i of the tile at k's 4(tid%32)..+3, Y chunk j is e = tid + 256j of the
+    // block's 32Q chunks.  Interior tiles (all TR rows inside R, all TK k's inside the
+    // split) copy by pointer adds alone; edge tiles take the per-chunk checks below.
+    constexpr int XCH = TR * TK / 4 / 256, YCH = (32 * Q + 255) / 256;
+    const bool rows_full = r0 + TR <= R;
+    const float* xrow = X + (r0 + (tid >> 5)) * x_sr + kb + 4 * (tid & 31);  // read only when rows_full
+    const int64_t xstep = 8 * x_sr;
+    const int xdst = (tid >> 5) * TK + 4 * (tid & 31);
+    int ydst[YCH];
+#pragma unroll
+    for (int j = 0; j < YCH; ++j) {
+        const int e = tid + 256 * j, g = e / Q;
+        ydst[j] = g * sk2_group_floats<Q>() + 4 * (e - g * Q);
+    }
+
     auto issue = [&](int t) {
         float* xs = sk2_smem_buf + (t % ST) * STAGE;
         const int64_t k0 = kb + static_cast<int64_t>(t) * TK;
+        if (rows_full && k0 + TK <= ke) {
+            const float* xp = xrow + static_cast<int64_t>(t) * TK;
 #pragma unroll
-        for (int i = 0; i < TR * TK / 4 / 256; ++i) {
+            for (int i = 0; i < XCH; ++i) cp_async16(xs + xdst + 8 * i * TK, xp + i * xstep, 16);
+            const float* yp = Y + k0 * Q;
+#pragma unroll
+            for (int j = 0; j < YCH; ++j)
+                if (tid + 256 * j < 32 * Q) cp_async16(xs + TR * TK + ydst[j], yp + 4 * (tid + 256 * j), 16);
+            return;
+        }
+#pragma unroll
+        for (int i = 0; i < XCH; ++i) {
             const int e = tid + i * 256;
             const int rr = e >> 5, c = e & 31;
             const int64_t r = r0 + rr, k = k0 + 4 * c;
@@ -599,12 +625,41 @@ __global__ void __launch_bounds__(256, 2) gemm_skinny_r2_kernel(
     C += static_cast<int64_t>(blockIdx.y) * c_sb;
     const int ntiles = ke > kb ? static_cast<int>((ke - kb + TK - 1) / TK) : 0;
 
+    // This thread's copy plan, fixed over the K range: X chunk i of a stage is k row
+    // tid/64 + 4i of the tile at r's 4(tid%64)..+3, Y element j is e = tid + 256j of the
+    // TK x QP block.  Interior tiles (all TR r's inside R, all TK k's inside the split)
+    // copy by pointer adds alone; edge tiles take the per-chunk checks below.
+    constexpr int XCH = TK * TR / 4 / 256, YCH = (TK * QP + 255) / 256;
+    const bool rows_full = r0 + TR <= R;
+    const float* xcol = X + (kb + (tid >> 6)) * x_sk + r0 + 4 * (tid & 63);  // read only when rows_full
+    const int64_t xstep = 4 * x_sk;
+    const int xdst = (tid >> 6) * TR + 4 * (tid & 63);
+    int64_t yoff[YCH];
+    bool yin[YCH];
+#pragma unroll
+    for (int j = 0; j < YCH; ++j) {
+        const int e = tid + 256 * j, kk = e / QP, q = e - kk * QP;
+        yin[j] = e < TK * QP && q < Q;
+        yoff[j] = kk * y_sk + q * y_sq;
+    }
+
     auto issue = [&](int t) {
         const int s = t % ST;
         float* xs = Xs + s * TK * TR;
         const int64_t k0 = kb + static_cast<int64_t>(t) * TK;
+        if (rows_full && k0 + TK <= ke) {
+            const float* xp = xcol + static_cast<int64_t>(t) * TK * x_sk;
 #pragma unroll
-        for (int i = 0; i < TK * TR / 4 / 256; ++i) {
+            for (int i = 0; i < XCH; ++i) cp_async16(xs + xdst + 4 * i * TR, xp + i * xstep, 16);
+            float* ys = Ys + s * TK * QP;
+            const float* yp = Y + k0 * y_sk;
+#pragma unroll
+            for (int j = 0; j < YCH; ++j)
+                if (tid + 256 * j < TK * QP) cp_async4(ys + tid + 256 * j, yin[j] ? yp + yoff[j] : Y, yin[j] ? 4 : 0);
+            return;
+        }
+#pragma unroll
+        for (int i = 0; i < XCH; ++i) {
             const int e = tid + i * 256;
             const int kk = e >> 6, c = e & 63;
             const int64_t k = k0 + kk, r = r0 + 4 * c;
