@@ -73,6 +73,9 @@ size_t mm_operand(const Region& r, int mm, int role) {
 // reads at the minimum four shared-memory wavefronts.  Tiles are numbered rows first,
 // so the CTAs resident together write neighbouring runs of each transposed row; one
 // CTA per tile (the hardware balances the SMs).
+#ifndef TT_TILED_MM_CTAS
+#define TT_TILED_MM_CTAS 5
+#endif
 static void emit_region_tiled(std::ostringstream& ss, const Plan& p, Region& r) {
     const Graph& g = p.g;
     const size_t next = r.ext.size(), nsto = r.store_ref.size();
@@ -93,11 +96,16 @@ static void emit_region_tiled(std::ostringstream& ss, const Plan& p, Region& r) 
     ss << "// region " << r.kernel << ": fused over " << shape_str(r.shape) << ", tiled, hi/lo copies of store " << cs
        << (r.copy_rows ? " [R][C]" : "") << (r.copy_t ? " [C][R]" : "") << (r.drop_f32 ? ", its fp32 not stored" : "")
        << "\n";
-    // A region that forms a small-K product would hold B's values for all four rows in
-    // registers (80 per thread, 3 CTAs per SM); capping it at 64 keeps 4 CTAs resident.
+    // A region that forms a small-K product holds the four rows' products and loads in
+    // registers; its launch bound asks for TT_TILED_MM_CTAS resident CTAs per SM.  Measured
+    // on the MLP's dZ2 region at [32768, 4096] (one box, two runs each): 4 CTAs 0.57-0.58 ms
+    // (64 registers), 5 CTAs 0.53-0.54 ms (48 registers and a few bytes of spill), 6 CTAs
+    // 0.56 ms (40 registers, more spill).
     bool has_mm = false;
     for (int i : r.nodes) has_mm |= g.nodes[static_cast<size_t>(i)].inline_mm;
-    ss << "extern \"C\" __global__ void __launch_bounds__(256" << (has_mm ? ", 4" : "") << ") " << r.kernel << "(";
+    ss << "extern \"C\" __global__ void __launch_bounds__(256";
+    if (has_mm) ss << ", " << TT_TILED_MM_CTAS;
+    ss << ") " << r.kernel << "(";
     for (size_t e = 0; e < next; ++e) ss << (e ? ", " : "") << "const float* __restrict__ x" << e;
     for (size_t k = 0; k < nsto; ++k) ss << (next + k ? ", " : "") << "float* __restrict__ y" << k;
     ss << ", float* __restrict__ ch, float* __restrict__ cl, float* __restrict__ th, float* __restrict__ tl) {\n";
@@ -175,27 +183,33 @@ static void emit_region_tiled(std::ostringstream& ss, const Plan& p, Region& r) 
         staged = true;
     }
     if (staged) ss << "  __syncthreads();\n";
+    // the four rows' products for the lane's four columns, k outermost: one float4 of B per
+    // k serves the four rows (B is not held for every k), and each element is still one
+    // sequential fmaf chain over k
+    for (int i : r.nodes) {
+        if (!g.nodes[static_cast<size_t>(i)].inline_mm) continue;
+        const int64_t K = r.ext_access[mm_operand(r, i, 1)].kcount;
+        ss << "  float pm" << i << "[4][4];\n";
+        ss << "#pragma unroll\n  for (int i = 0; i < 4; ++i)\n#pragma unroll\n    for (int l = 0; l < 4; ++l) pm" << i
+           << "[i][l] = 0.0f;\n";
+        ss << "#pragma unroll\n  for (int k = 0; k < " << K << "; ++k) {\n";
+        ss << "    const float4 bv = *reinterpret_cast<const float4*>(&sb" << i << "[k][4 * lane]);\n";
+        ss << "#pragma unroll\n    for (int i = 0; i < 4; ++i) {\n";
+        ss << "      const float av = sa" << i << "[w + 8 * i][k];\n";
+        ss << "      pm" << i << "[i][0] = fmaf(av, bv.x, pm" << i << "[i][0]); pm" << i << "[i][1] = fmaf(av, bv.y, pm" << i
+           << "[i][1]);\n";
+        ss << "      pm" << i << "[i][2] = fmaf(av, bv.z, pm" << i << "[i][2]); pm" << i << "[i][3] = fmaf(av, bv.w, pm" << i
+           << "[i][3]);\n    }\n  }\n";
+    }
     ss << "#pragma unroll\n  for (int i = 0; i < 4; ++i) {\n";
     ss << "    const I rr = r0 + w + 8 * i;\n";
     ss << "    const bool rin = rr < (I)" << R << ", full = rin && c + 3 < (I)" << C << ";\n";
-    for (int i : r.nodes) {  // this row's products for the lane's four columns
-        if (!g.nodes[static_cast<size_t>(i)].inline_mm) continue;
-        const int64_t K = r.ext_access[mm_operand(r, i, 1)].kcount;
-        ss << "    float pm" << i << "[4] = {0.0f, 0.0f, 0.0f, 0.0f};\n";
-        ss << "#pragma unroll\n    for (int k = 0; k < " << K << "; ++k) {  // one sequential fmaf chain per element\n";
-        ss << "      const float av = sa" << i << "[w + 8 * i][k];\n";
-        ss << "      const float4 bv = *reinterpret_cast<const float4*>(&sb" << i << "[k][4 * lane]);\n";
-        ss << "      pm" << i << "[0] = fmaf(av, bv.x, pm" << i << "[0]); pm" << i << "[1] = fmaf(av, bv.y, pm" << i
-           << "[1]);\n";
-        ss << "      pm" << i << "[2] = fmaf(av, bv.z, pm" << i << "[2]); pm" << i << "[3] = fmaf(av, bv.w, pm" << i
-           << "[3]);\n    }\n";
-    }
     for (size_t k = 0; k < nsto; ++k) ss << "    float o" << k << "[4];\n";
     ss << "#pragma unroll\n    for (int l = 0; l < 4; ++l) {\n";
     for (int i : r.nodes) {
         const Node& nd = g.nodes[static_cast<size_t>(i)];
         if (nd.inline_mm) {  // formed above: one sequential fmaf chain over k per element
-            ss << "      const float v" << i << " = pm" << i << "[l];\n";
+            ss << "      const float v" << i << " = pm" << i << "[i][l];\n";
             continue;
         }
         ss << "      const float v" << i << " = "
