@@ -234,6 +234,7 @@ class CompiledProgram:
         self._grad_nodes = list(grad_nodes)
         self._h = handle
         self._inputs = graph.inputs
+        self._dev_args = None  # (input pointers, output pointers, their ctypes arrays) of the last run_device
         ni, no = ctypes.c_int32(), ctypes.c_int32()
         _lib.check(_lib.lib.tt_program_num_io(self._h, ctypes.byref(ni), ctypes.byref(no)))
         self.num_inputs, self.num_outputs = ni.value, no.value
@@ -304,15 +305,18 @@ class CompiledProgram:
         if len(outputs) != self.num_outputs:
             raise RuntimeExecutionError(f"Expected {self.num_outputs} outputs, but got {len(outputs)}")
         # the pointer arrays of the last call are reused when the buffers repeat (a loop over
-        # the same buffers pays for building them once: ~2 us of a launch-bound call)
-        key = (tuple(getattr(x, "ptr", x) for x in inputs), tuple(getattr(x, "ptr", x) for x in outputs))
-        cached = getattr(self, "_dev_args", None)
-        if cached is None or cached[0] != key:
-            ip = (ctypes.c_void_p * max(1, len(inputs)))(*key[0])
-            op = (ctypes.c_void_p * max(1, len(outputs)))(*key[1])
-            cached = self._dev_args = (key, ip, op)
+        # the same buffers pays for building them once: ~2 us of a launch-bound call); the
+        # pointer lists are list comprehensions, ~0.5 us cheaper per call than tuples of
+        # generators
+        ki = [getattr(x, "ptr", x) for x in inputs]
+        ko = [getattr(x, "ptr", x) for x in outputs]
+        cached = self._dev_args
+        if cached is None or cached[0] != ki or cached[1] != ko:
+            ip = (ctypes.c_void_p * max(1, len(ki)))(*ki)
+            op = (ctypes.c_void_p * max(1, len(ko)))(*ko)
+            cached = self._dev_args = (ki, ko, ip, op)
         h = stream.handle if isinstance(stream, Stream) else stream
-        _lib.check(_lib.lib.tt_program_run(self._h, cached[1], cached[2], _lib.DEVICE, h))
+        _lib.check(_lib.lib.tt_program_run(self._h, cached[2], cached[3], _lib.DEVICE, h))
 
     def status(self) -> int:
         """Synchronises and returns the device status word (raises if a kernel gave up)."""

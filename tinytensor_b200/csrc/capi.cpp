@@ -107,6 +107,9 @@ struct tt_program {
     cudaStream_t side = nullptr;          // second stream for concurrent GEMM pairs
     cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     std::mutex run_mutex;
+    // per-run scratch, reused under run_mutex so a run allocates no host memory after the first
+    std::vector<char*> in_ptr, out_ptr;
+    std::vector<void*> arg_vals, arg_ptrs;
 
     ~tt_program() {
         for (cudaEvent_t e : events) cudaEventDestroy(e);
@@ -347,8 +350,8 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
         if (L.type == LT_REGION) {
             const Region& r = pl.regions[static_cast<size_t>(L.region)];
             if (r.grid > 0) {
-                std::vector<void*> vals;
-                vals.reserve(r.ext.size() + r.store_ref.size() + 4);
+                std::vector<void*>& vals = p->arg_vals;
+                vals.clear();
                 for (size_t e = 0; e < r.ext.size(); ++e) {
                     const Access& a = r.ext_access[e];
                     vals.push_back(a.imm ? nullptr : resolve(pl.root_ref[static_cast<size_t>(a.node)]));
@@ -362,7 +365,8 @@ static void run_launches(tt_program* p, char* const* in_ptr, char* const* out_pt
                                                ? base + split_copies_offset(r.copy_R, r.copy_C, r.copy_rows, layout, lo)
                                                : nullptr);
                 }
-                std::vector<void*> args(vals.size());
+                std::vector<void*>& args = p->arg_ptrs;
+                args.resize(vals.size());
                 for (size_t i = 0; i < vals.size(); ++i) args[i] = &vals[i];
                 CUresult cr = driver().launchKernel(p->region_fn[static_cast<size_t>(L.region)],
                                                     static_cast<unsigned>(r.grid), 1, 1, 256, 1, 1, 0, st,
@@ -438,7 +442,10 @@ int tt_program_run(tt_program* p, const void* const* inputs, void* const* output
         cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
         if (p->device < 0) fail(TT_ERR_NO_DEVICE, "program was compiled host-only (TT_FLAG_HOST_ONLY)");
         check_cuda(cudaSetDevice(p->device), "cudaSetDevice");
-        std::vector<char*> in_ptr(ni), out_ptr(no);
+        std::vector<char*>& in_ptr = p->in_ptr;
+        std::vector<char*>& out_ptr = p->out_ptr;
+        in_ptr.assign(ni, nullptr);
+        out_ptr.assign(no, nullptr);
         for (size_t k = 0; k < ni; ++k)
             if (!inputs[k] && p->in_bytes[k]) fail(TT_ERR_RUNTIME, "Input " + std::to_string(k) + " is null");
         for (size_t k = 0; k < no; ++k)
