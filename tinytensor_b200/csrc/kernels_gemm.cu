@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(256, SK2_RW <= 4 ? 2 : 1) gemm_skinny_k2_kerne
     // split) copy by pointer adds alone; edge tiles take the per-chunk checks below.
     constexpr int XCH = TR * TK / 4 / 256, YCH = (32 * Q + 255) / 256;
     const bool rows_full = r0 + TR <= R;
-    const float* xrow = X + (r0 + (tid >> 5)) * x_sr + kb + 4 * (tid & 31);  // read only when rows_full
+    const float* xrow = rows_full ? X + (r0 + (tid >> 5)) * x_sr + kb + 4 * (tid & 31) : X;
     const int64_t xstep = 8 * x_sr;
     const int xdst = (tid >> 5) * TK + 4 * (tid & 31);
     int ydst[YCH];
@@ -631,7 +631,7 @@ __global__ void __launch_bounds__(256, 2) gemm_skinny_r2_kernel(
     // copy by pointer adds alone; edge tiles take the per-chunk checks below.
     constexpr int XCH = TK * TR / 4 / 256, YCH = (TK * QP + 255) / 256;
     const bool rows_full = r0 + TR <= R;
-    const float* xcol = X + (kb + (tid >> 6)) * x_sk + r0 + 4 * (tid & 63);  // read only when rows_full
+    const float* xcol = rows_full ? X + (kb + (tid >> 6)) * x_sk + r0 + 4 * (tid & 63) : X;
     const int64_t xstep = 4 * x_sk;
     const int xdst = (tid >> 6) * TR + 4 * (tid & 63);
     int64_t yoff[YCH];
