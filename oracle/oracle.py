@@ -262,6 +262,13 @@ def magnitude(graph, feed, outputs=None):
                 v, mg = x[0].reshape(n.shape), m[0].reshape(n.shape)
             elif op == EXPAND:
                 v, mg = np.broadcast_to(x[0], n.shape), np.broadcast_to(m[0], n.shape)
+            elif op in (REDUCE_SUM, REDUCE_MEAN, REDUCE_MAX):
+                rank = x[0].ndim
+                ax = tuple(sorted(set(range(rank)) if not n.axes else {a % rank for a in n.axes}))
+                f = {REDUCE_SUM: np.sum, REDUCE_MEAN: np.mean, REDUCE_MAX: np.max}[op]
+                v, mg = f(x[0], axis=ax, keepdims=n.keepdims), f(m[0], axis=ax, keepdims=n.keepdims)
+            elif op == MATMUL:
+                v, mg = np.matmul(x[0], x[1]), np.matmul(m[0], m[1])
             else:
                 raise ValueError(f"magnitude: unsupported op {op}")
         vals[n.index], mags[n.index] = v, mg

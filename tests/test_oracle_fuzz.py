@@ -1,0 +1,119 @@
+"""Pins the CPU oracle to the reference beyond the golden cases: seeded random graphs
+(broadcasting elementwise chains with scalar constants, IEEE special values, reductions
+over random axes with and without keepdims, transposes, 2-D and batched matmuls) run
+through the oracle restatement (oracle/tt_oracle.c) and through the reference's own
+interpreter (oracle/_ref, built from the reference sources), compared bit for bit.
+No GPU needed."""
+
+import numpy as np
+import pytest
+
+from parity import assert_bitexact
+
+import tinytensor_b200 as tt
+from oracle import oracle as O
+
+pytestmark = pytest.mark.skipif(not O.reference_available(), reason="oracle/_ref not built")
+
+SPECIALS = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-38, -3e38, 1.0, -1.0], np.float32)
+
+
+# without values near the float maximum: sums of products then never overflow, so their
+# non-finite classes do not depend on the summation order
+SPECIALS_NO_OVERFLOW = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-38, 1.0, -1.0], np.float32)
+
+
+def _values(rng, shape, special, specials=SPECIALS):
+    x = rng.standard_normal(shape).astype(np.float32) * np.float32(rng.choice([0.1, 1.0, 30.0]))
+    if special and x.size:
+        mask = rng.random(shape) < 0.15
+        x[mask] = rng.choice(specials, size=int(mask.sum()))
+    return x
+
+
+def _derived(rng, base):
+    """A shape that broadcasts against `base`: some dims set to 1, leading dims dropped."""
+    s = [d if rng.random() < 0.6 else 1 for d in base]
+    return s[int(rng.integers(0, len(s))):] if len(s) > 1 and rng.random() < 0.3 else s
+
+
+def _elementwise_case(seed):
+    rng = np.random.default_rng(seed)
+    rank = int(rng.integers(1, 4))
+    base = [int(rng.integers(1, 7)) for _ in range(rank)]
+    g = tt.Graph()
+    shapes = [base] + [_derived(rng, base) for _ in range(int(rng.integers(1, 3)))]
+    ins = [g.input(s) for s in shapes]
+    pool = list(ins)
+    for _ in range(int(rng.integers(3, 8))):
+        k = int(rng.integers(0, 8))
+        a = pool[int(rng.integers(0, len(pool)))]
+        b = pool[int(rng.integers(0, len(pool)))]
+        if k == 0:
+            y = a + b
+        elif k == 1:
+            y = a - b
+        elif k == 2:
+            y = a * b
+        elif k == 3:
+            y = a / b
+        elif k == 4:
+            y = tt.relu(a)
+        elif k == 5:
+            y = tt.sigmoid(a)
+        elif k == 6:
+            y = a * float(rng.choice([0.5, -2.0, 3.0]))
+        else:
+            y = a + float(rng.choice([1.0, -0.25]))
+        pool.append(y)
+    y = pool[-1]
+    outs = [y]
+    if len(y.shape) >= 2 and rng.random() < 0.4:
+        d0, d1 = (int(v) for v in rng.choice(len(y.shape), size=2, replace=False))
+        outs.append(tt.transpose(y, d0, d1))
+    if len(y.shape) >= 1 and rng.random() < 0.7:
+        nax = int(rng.integers(1, len(y.shape) + 1))
+        axes = sorted(int(v) for v in rng.choice(len(y.shape), size=nax, replace=False))
+        red = tt.sum if rng.random() < 0.5 else tt.mean
+        outs.append(red(y, axes, keepdims=bool(rng.random() < 0.5)))
+    for o in outs:
+        g.mark_output(o)
+    special = rng.random() < 0.5
+    feed = {n: _values(rng, n.shape, special) for n in ins}
+    return g, feed
+
+
+def _matmul_case(seed, specials=SPECIALS):
+    rng = np.random.default_rng(seed)
+    m, k, n = (int(v) for v in rng.integers(1, 40, size=3))
+    g = tt.Graph()
+    if rng.random() < 0.3:
+        bsz = int(rng.integers(1, 4))
+        a, b = g.input([bsz, m, k]), g.input([bsz, k, n])
+    else:
+        a, b = g.input([m, k]), g.input([k, n])
+    y = a @ b
+    g.mark_output(y)
+    if rng.random() < 0.5:
+        g.mark_output(tt.relu(y + 0.5))
+    if len(y.shape) == 2 and rng.random() < 0.5:
+        g.mark_output(tt.sum(tt.transpose(y, 0, 1), [1]))
+    special = rng.random() < 0.3
+    feed = {x: _values(rng, x.shape, special, specials) for x in (a, b)}
+    return g, feed
+
+
+@pytest.mark.parametrize("seed", range(200))
+def test_elementwise_and_reduction_graphs_match_reference_interpreter(seed):
+    g, feed = _elementwise_case(1000 + seed)
+    ref = O.Reference().run(g, feed, mode="interpreted")
+    for got, r in zip(O.evaluate(g, feed), ref):
+        assert_bitexact(got, r)
+
+
+@pytest.mark.parametrize("seed", range(60))
+def test_matmul_graphs_match_reference_interpreter(seed):
+    g, feed = _matmul_case(5000 + seed)
+    ref = O.Reference().run(g, feed, mode="interpreted")
+    for got, r in zip(O.evaluate(g, feed), ref):
+        assert_bitexact(got, r)
