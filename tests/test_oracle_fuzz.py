@@ -2,7 +2,9 @@
 (broadcasting elementwise chains with scalar constants, IEEE special values, reductions
 over random axes with and without keepdims, transposes, 2-D and batched matmuls) run
 through the oracle restatement (oracle/tt_oracle.c) and through the reference's own
-interpreter (oracle/_ref, built from the reference sources), compared bit for bit.
+interpreter (oracle/_ref, built from the reference sources), compared bit for bit;
+and random differentiable graphs whose gradients are compared with the reference's
+Autodiff::compute_gradients (src/autodiff/gradient.cpp:52-332) bit for bit.
 No GPU needed."""
 
 import numpy as np
@@ -116,4 +118,53 @@ def test_matmul_graphs_match_reference_interpreter(seed):
     g, feed = _matmul_case(5000 + seed)
     ref = O.Reference().run(g, feed, mode="interpreted")
     for got, r in zip(O.evaluate(g, feed), ref):
+        assert_bitexact(got, r)
+
+
+def _gradient_case(seed):
+    """A random differentiable graph with a scalar loss: an elementwise chain over
+    broadcasting inputs, or a two-layer perceptron with random activations, reduced by
+    sum or mean over every axis."""
+    rng = np.random.default_rng(seed)
+    g = tt.Graph()
+    if rng.random() < 0.5:
+        rank = int(rng.integers(1, 4))
+        base = [int(rng.integers(1, 6)) for _ in range(rank)]
+        ins = [g.input(base)] + [g.input(_derived(rng, base)) for _ in range(int(rng.integers(1, 3)))]
+        pool = list(ins)
+        for _ in range(int(rng.integers(2, 6))):
+            k = int(rng.integers(0, 7))
+            a = pool[int(rng.integers(0, len(pool)))]
+            b = pool[int(rng.integers(0, len(pool)))]
+            y = (a + b, a - b, a * b, a / b, tt.relu(a), tt.sigmoid(a), a * 0.5)[k]
+            pool.append(y)
+        y = pool[-1]
+        if len(y.shape) >= 2 and rng.random() < 0.3:
+            y = tt.transpose(y, 0, len(y.shape) - 1) * 2.0
+    else:
+        m, k, h, n = (int(v) for v in rng.integers(1, 12, size=4))
+        x, w1, b1, w2 = g.input([m, k]), g.input([k, h]), g.input([h]), g.input([h, n])
+        ins = [x, w1, b1, w2]
+        act = tt.relu if rng.random() < 0.5 else tt.sigmoid
+        y = act(x @ w1 + b1) @ w2
+        if rng.random() < 0.5:
+            t = g.input([m, n])
+            ins.append(t)
+            y = (y - t) * (y - t)
+    loss = tt.sum(y) if rng.random() < 0.5 else tt.mean(y)
+    feed = {n: _values(rng, n.shape, rng.random() < 0.3) for n in ins}
+    reach, stack = set(), [loss]
+    while stack:  # the inputs the loss depends on: the ones a gradient reaches
+        n = stack.pop()
+        if n.index not in reach:
+            reach.add(n.index)
+            stack.extend(n.inputs)
+    return g, loss, [n for n in ins if n.index in reach], feed
+
+
+@pytest.mark.parametrize("seed", range(80))
+def test_gradients_match_reference_autodiff(seed):
+    g, loss, wrt, feed = _gradient_case(9000 + seed)
+    ref = O.Reference().gradients(g, loss, feed, wrt)
+    for got, r in zip(O.gradients(g, loss, feed, wrt), ref):
         assert_bitexact(got, r)
