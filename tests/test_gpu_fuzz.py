@@ -1,10 +1,11 @@
 """GPU parity on seeded random graphs: the graphs of the oracle's reference cross-check
 (broadcasting elementwise chains with scalar constants and IEEE special values,
 reductions over random axes with and without keepdims, transposes, 2-D and batched
-matmuls) compiled for the B200 and run through the C ABI, held to the oracle with the
-parity contract's tolerances: bit-exact for chains of + - * / relu and for transposes
-of them, the transcendental bound where sigmoid appears, norm-wise for reductions and
-products, with NaN / inf patterns equal everywhere."""
+matmuls, and random differentiable graphs through their compiled backward pass)
+compiled for the B200 and run through the C ABI, held to the oracle with the parity
+contract's tolerances: bit-exact for chains of + - * / relu and for transposes of them,
+the transcendental bound where sigmoid appears, norm-wise for reductions, products and
+gradients, with NaN / inf patterns equal everywhere."""
 
 import numpy as np
 import pytest
@@ -16,7 +17,7 @@ from parity import (
     assert_elementwise_scaled,
     assert_norm,
 )
-from test_oracle_fuzz import SPECIALS_NO_OVERFLOW, _elementwise_case, _matmul_case
+from test_oracle_fuzz import SPECIALS_NO_OVERFLOW, _elementwise_case, _gradient_case, _matmul_case
 
 import tinytensor_b200 as tt
 from oracle import oracle as O
@@ -66,4 +67,14 @@ def test_matmul_graphs(seed, cache_dir):
     res = prog.run(feed)
     got = [r.numpy() for r in (res if isinstance(res, list) else [res])]
     for gv, ov in zip(got, O.evaluate(g, feed, outs)):
+        _assert_classes_then_norm(gv, ov, GEMM_FROB_RTOL)
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_gradient_graphs(seed, cache_dir):
+    g, loss, wrt, feed = _gradient_case(9000 + seed, SPECIALS_NO_OVERFLOW)
+    prog = tt.compile_gradients(g, loss, wrt, cache_dir=cache_dir)
+    got = [r.numpy() for r in prog.run(feed)[1:]]
+    assert len(got) == len(wrt)
+    for gv, ov in zip(got, O.gradients(g, loss, feed, wrt)):
         _assert_classes_then_norm(gv, ov, GEMM_FROB_RTOL)

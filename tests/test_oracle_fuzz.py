@@ -121,7 +121,7 @@ def test_matmul_graphs_match_reference_interpreter(seed):
         assert_bitexact(got, r)
 
 
-def _gradient_case(seed):
+def _gradient_case(seed, specials=SPECIALS):
     """A random differentiable graph with a scalar loss: an elementwise chain over
     broadcasting inputs, or a two-layer perceptron with random activations, reduced by
     sum or mean over every axis."""
@@ -152,7 +152,7 @@ def _gradient_case(seed):
             ins.append(t)
             y = (y - t) * (y - t)
     loss = tt.sum(y) if rng.random() < 0.5 else tt.mean(y)
-    feed = {n: _values(rng, n.shape, rng.random() < 0.3) for n in ins}
+    feed = {n: _values(rng, n.shape, rng.random() < 0.3, specials) for n in ins}
     reach, stack = set(), [loss]
     while stack:  # the inputs the loss depends on: the ones a gradient reaches
         n = stack.pop()
