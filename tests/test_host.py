@@ -395,6 +395,26 @@ def test_small_k_product_is_formed_inside_its_region(cache_dir):
     assert "simt_smallk" in _host_compile(g2, [m, m * 3.0], cache_dir).execution_plan()
 
 
+def test_tiled_small_k_region_forms_the_product_k_outermost(cache_dir):
+    """The tiled dZ2 region forms its K = 10 product with k outermost (one float4 of B per
+    k for the tile's four rows) and asks for 5 resident CTAs per SM; the 10-wide output
+    and weight-gradient GEMMs take the skinny kernels."""
+    g = tt.Graph()
+    x, t = g.input([4096, 1024]), g.input([4096, 10])
+    w1, w2, w3 = g.input([1024, 4096]), g.input([4096, 4096]), g.input([4096, 10])
+    d = tt.tanh(tt.relu(x @ w1) @ w2) @ w3 - t
+    p = tt.compile_gradients(g, tt.mean(d * d), [w1, w2, w3], cache_dir=cache_dir, flags=HOST)
+    src, plan = p.generated_source(), p.execution_plan()
+    tiled = [k for k in src.split("extern \"C\" __global__")[1:] if "sb" in k and "tile[32][132]" in k]
+    assert len(tiled) == 1, plan
+    body = tiled[0]
+    assert body.startswith(" void __launch_bounds__(256, 5)"), body[:80]
+    # the k loop sits between the row loads and the per-row loop that uses the products
+    rows = "const I rr = r0 + w + 8 * i;"
+    assert body.index(rows) < body.index("for (int k = 0; k < 10; ++k)") < body.rindex(rows)
+    assert plan.count("simt_skinny[") == 2, plan
+
+
 def _region_variant_graphs():
     """Graphs whose regions use every generated-kernel variant of the GEMM-adjacent
     fusion: tiled regions writing one or both copy layouts (with and without the fp32
