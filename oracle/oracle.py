@@ -64,7 +64,10 @@ _o = _load_oracle()
 
 
 def _f32(a):
-    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+    # not np.ascontiguousarray alone: it returns at least 1-d, and a rank-0 value must
+    # stay rank 0 (shape ()), as the reference's scalar tensors do
+    a = np.asarray(a, dtype=np.float32)
+    return a if a.flags.c_contiguous else np.ascontiguousarray(a)
 
 
 def _shape(a):

@@ -168,3 +168,23 @@ def test_gradients_match_reference_autodiff(seed):
     ref = O.Reference().gradients(g, loss, feed, wrt)
     for got, r in zip(O.gradients(g, loss, feed, wrt), ref):
         assert_bitexact(got, r)
+
+
+@pytest.mark.parametrize("shape", [[], [0], [0, 3], [2, 0], [1], [3, 1, 2]])
+def test_rank0_and_empty_shapes_match_reference_interpreter(shape):
+    """Rank-0 values stay rank 0 and empty extents give the reference's shapes and values
+    (sums of nothing are 0) through elementwise ops, scalar constants and reductions."""
+    g = tt.Graph()
+    a, b = g.input(shape), g.input(shape)
+    y = tt.relu(a * b + 1.0)
+    outs = [y, tt.sigmoid(y) - 0.5 * a]
+    if shape:
+        outs += [tt.sum(y, [0]), tt.mean(y, [0], keepdims=True)]
+    outs += [tt.sum(y), tt.mean(y * b)]
+    for o in outs:
+        g.mark_output(o)
+    feed = {a: np.full(shape, 2.0, np.float32), b: np.full(shape, -3.0, np.float32)}
+    ref = O.Reference().run(g, feed, mode="interpreted")
+    got = O.evaluate(g, feed)
+    for x, r in zip(got, ref):
+        assert_bitexact(x, r)
