@@ -188,3 +188,42 @@ def test_rank0_and_empty_shapes_match_reference_interpreter(shape):
     got = O.evaluate(g, feed)
     for x, r in zip(got, ref):
         assert_bitexact(x, r)
+
+
+def _edge_graphs():
+    """Shape edge cases of the reference's builders and kernels."""
+    cases = {
+        "negative transpose dims": lambda g: (lambda a: ([a], [tt.transpose(a, -1, 0), tt.transpose(a, 1, -1)]))(
+            g.input([2, 3, 4])),
+        "negative reduce axes": lambda g: (lambda a: ([a], [tt.sum(a, [-1]), tt.mean(a, [-3, -1], keepdims=True),
+                                                             tt.sum(a, [0, 2])]))(g.input([2, 3, 4])),
+        "zero extent broadcast": lambda g: (lambda a, b: ([a, b], [a + b]))(g.input([0, 1]), g.input([1, 5])),
+        "matmul with K = 0": lambda g: (lambda a, b: ([a, b], [a @ b]))(g.input([4, 0]), g.input([0, 3])),
+        "batched matmul, broadcast batch": lambda g: (lambda a, b: ([a, b], [a @ b]))(g.input([1, 3, 4]),
+                                                                                      g.input([5, 4, 2])),
+        "batched matmul, unequal batch ranks": lambda g: (lambda a, b: ([a, b], [a @ b]))(g.input([2, 1, 3, 4]),
+                                                                                          g.input([5, 4, 2])),
+        "x / 0": lambda g: (lambda a: ([a], [a / (a - a)]))(g.input([3])),
+        "reduction of a transpose": lambda g: (lambda a: ([a], [tt.sum(tt.transpose(a, 0, 1), [0], keepdims=True)
+                                                                 / 3.0]))(g.input([2, 3])),
+    }
+    return cases
+
+
+@pytest.mark.parametrize("name", sorted(_edge_graphs()))
+def test_shape_edge_cases_match_reference_interpreter(name):
+    g = tt.Graph()
+    ins, outs = _edge_graphs()[name](g)
+    for o in outs:
+        g.mark_output(o)
+    rng = np.random.default_rng(7)
+    feed = {n: rng.standard_normal(n.shape).astype(np.float32) for n in ins}
+    ref = O.Reference().run(g, feed, mode="interpreted")
+    for x, r in zip(O.evaluate(g, feed), ref):
+        assert_bitexact(x, r)
+
+
+def test_matmul_rank_rules_match_reference():
+    g = tt.Graph()
+    with pytest.raises(tt.DimensionError, match="Unsupported ranks for matmul"):
+        g.input([3, 4]) @ g.input([4])
